@@ -1,0 +1,259 @@
+/* lc_b200.h -- C ABI of liblc_b200.so, the B200 (sm_100a) build of Lightning Core's
+ * attention / matmul2d / conv->attention hot path.
+ *
+ * Part 1 keeps every runtime symbol, enum and struct of the reference's C ABI with identical
+ * names, values and layouts (include/lightning_core/lightning_core.h:1-141 of the reference;
+ * implementation src/lightning_core_c_api.cpp:179-353), so existing C callers relink unchanged.
+ * Part 2 adds the op entry points the reference only exposes through C++ templates and pybind.
+ *
+ * Conventions of the op entry points (part 2):
+ *  - Errors are returned as lcError_t, never thrown.  Null or zero-sized arguments ->
+ *    LC_INVALID_VALUE (reference: src/attention.cpp:145-148, ops.hpp:366-369); a shape the
+ *    kernels cannot take -> LC_NOT_SUPPORTED; a CUDA failure or a kernel-side bounded wait that
+ *    gave up -> LC_DRIVER_ERROR.  There is no CPU fallback on any path.
+ *  - IO policies carry the reference's meaning on explicit device memory: an upload_* flag set
+ *    means that pointer is HOST memory and is copied in with cudaMemcpyAsync; clear means it
+ *    is already a DEVICE pointer (or, for sessions, that the session's resident buffer is
+ *    reused).  download_out set means `out` is host memory and the result is copied back;
+ *    synchronize set means cudaStreamSynchronize(stream) before returning.  A NULL policy
+ *    means "all device pointers, asynchronous".
+ *  - `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *  - Tensors are dense row-major; "units" are independent heads/images stacked outermost.
+ */
+#ifndef LC_B200_H
+#define LC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#define LC_API_VERSION_MAJOR 0
+#define LC_API_VERSION_MINOR 6
+#define LC_API_VERSION_PATCH 0
+#define LC_API_VERSION_STRING "0.6.0-rc0"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ===================== Part 1: reference runtime ABI (lightning_core.h) ================= */
+
+typedef enum lcError {
+  LC_SUCCESS = 0,
+  LC_NOT_INITIALIZED,
+  LC_INVALID_VALUE,
+  LC_OUT_OF_MEMORY,
+  LC_NOT_SUPPORTED,
+  LC_DRIVER_ERROR,
+  LC_UNKNOWN
+} lcError_t;
+
+typedef enum lcMemcpyKind {
+  LC_MEMCPY_HOST_TO_HOST = 0,
+  LC_MEMCPY_HOST_TO_DEVICE,
+  LC_MEMCPY_DEVICE_TO_HOST,
+  LC_MEMCPY_DEVICE_TO_DEVICE
+} lcMemcpyKind;
+
+typedef enum lcDeviceKind { LC_DEVICE_CPU = 0, LC_DEVICE_CUDA, LC_DEVICE_METAL } lcDeviceKind;
+
+typedef enum lcMemoryModel { LC_MEMORY_NATIVE_DEVICE = 0, LC_MEMORY_HOST_MANAGED_COMPAT } lcMemoryModel;
+
+typedef enum lcSyncMode { LC_SYNC_AUTO = 0, LC_SYNC_ALWAYS, LC_SYNC_NEVER } lcSyncMode;
+
+typedef struct lcSyncPolicy {
+  lcSyncMode mode;
+  int trace_sync_boundary;
+} lcSyncPolicy;
+
+typedef struct lcBackendCapabilities {
+  lcDeviceKind device;
+  int built;
+  int available;
+  int compute_surface;
+  int memory_surface;
+  int sync_surface;
+  int profiling_surface;
+  int runtime_trace_surface;
+  int sync_policy_surface;
+  lcMemoryModel memory_model;
+} lcBackendCapabilities;
+
+typedef struct lcComputeInterfaceContract {
+  int available;
+  int op_dispatch_trace_surface;
+  const char* driver_tag;
+} lcComputeInterfaceContract;
+
+typedef struct lcMemoryInterfaceContract {
+  int available;
+  int allocator_surface;
+  int memcpy_surface;
+  lcMemoryModel memory_model;
+  const char* driver_tag;
+} lcMemoryInterfaceContract;
+
+typedef struct lcSyncInterfaceContract {
+  int available;
+  int sync_policy_surface;
+  int trace_sync_boundary_surface;
+  const char* driver_tag;
+} lcSyncInterfaceContract;
+
+typedef struct lcProfilerInterfaceContract {
+  int available;
+  int runtime_trace_surface;
+  int op_dispatch_trace_surface;
+  size_t trace_capacity;
+  const char* driver_tag;
+} lcProfilerInterfaceContract;
+
+typedef struct lcBackendInterfaceContract {
+  lcDeviceKind device;
+  lcBackendCapabilities capabilities;
+  lcComputeInterfaceContract compute;
+  lcMemoryInterfaceContract memory;
+  lcSyncInterfaceContract sync;
+  lcProfilerInterfaceContract profiler;
+} lcBackendInterfaceContract;
+
+typedef enum lcStructId {
+  LC_STRUCT_BACKEND_CAPABILITIES = 1,
+  LC_STRUCT_COMPUTE_INTERFACE_CONTRACT = 2,
+  LC_STRUCT_MEMORY_INTERFACE_CONTRACT = 3,
+  LC_STRUCT_SYNC_INTERFACE_CONTRACT = 4,
+  LC_STRUCT_PROFILER_INTERFACE_CONTRACT = 5,
+  LC_STRUCT_BACKEND_INTERFACE_CONTRACT = 6
+} lcStructId;
+
+/* lightning_core.h:113-137 (reference). lcMalloc is cudaMalloc on the current device. */
+lcError_t lcMalloc(void** ptr, size_t size_bytes);
+lcError_t lcFree(void* ptr);
+lcError_t lcMemcpy(void* dst, const void* src, size_t size_bytes, lcMemcpyKind kind);
+lcError_t lcDeviceSynchronize(void);
+lcError_t lcGetDeviceCount(int* count);
+lcError_t lcGetPreferredDeviceForInference(lcDeviceKind* device);
+lcError_t lcGetPreferredDeviceForTraining(lcDeviceKind* device);
+int lcIsCudaAvailable(void);
+int lcIsMetalAvailable(void);
+lcMemoryModel lcGetMemoryModel(void);
+const char* lcGetMemoryModelName(lcMemoryModel model);
+lcError_t lcSetDefaultSyncPolicy(lcSyncPolicy policy);
+lcSyncPolicy lcGetDefaultSyncPolicy(void);
+lcError_t lcApplySyncPolicy(lcSyncPolicy policy);
+lcError_t lcApplyDefaultSyncPolicy(void);
+lcError_t lcGetBackendCapabilities(lcDeviceKind device, lcBackendCapabilities* out_caps);
+lcError_t lcGetActiveBackendCapabilities(lcBackendCapabilities* out_caps);
+lcError_t lcGetBackendInterfaceContract(lcDeviceKind device, lcBackendInterfaceContract* out_contract);
+lcError_t lcGetActiveBackendInterfaceContract(lcBackendInterfaceContract* out_contract);
+lcError_t lcGetApiVersion(int* out_major, int* out_minor, int* out_patch);
+const char* lcGetApiVersionString(void);
+size_t lcGetStructSize(lcStructId struct_id);
+int lcCheckStructSize(lcStructId struct_id, size_t observed_size);
+const char* lcBackendName(void);
+const char* lcGetErrorString(lcError_t error);
+
+/* ===================== Part 2: hot-path op entry points (new in this build) =============== */
+
+typedef enum lcDataType {
+  LC_DTYPE_F32 = 0,  /* fp32 in/out, strict fp32 arithmetic (SIMT FFMA)              */
+  LC_DTYPE_BF16 = 1, /* bf16 in/out, fp32 accumulate/softmax on tcgen05 tensor cores */
+  LC_DTYPE_F64 = 2   /* vector add only                                             */
+} lcDataType;
+
+typedef void* lcStream_t; /* a cudaStream_t */
+
+/* include/lightning_core/core/attention.hpp:16-32 (AttentionIoPolicy), ints for bools. */
+typedef struct lcAttentionIoPolicy {
+  int upload_q, upload_k, upload_v, upload_target;
+  int download_out, download_v, synchronize;
+  int loss_every;
+  float output_scale, output_bias; /* out = max(0?)(out*scale + bias), relu if output_relu */
+  int output_relu;
+} lcAttentionIoPolicy;
+
+/* include/lightning_core/core/ops/policy.hpp:8-34. */
+typedef struct lcMatMulIoPolicy { int upload_a, upload_b, download_out, synchronize; } lcMatMulIoPolicy;
+typedef struct lcVectorAddIoPolicy { int upload_a, upload_b, download_out, synchronize; } lcVectorAddIoPolicy;
+typedef struct lcConv2dIoPolicy { int upload_x, upload_w, upload_bias, download_out, synchronize; } lcConv2dIoPolicy;
+
+/* Fills the reference defaults (everything true, loss_every=1, scale 1, bias 0, no relu). */
+void lcAttentionIoPolicyDefault(lcAttentionIoPolicy* p);
+void lcMatMulIoPolicyDefault(lcMatMulIoPolicy* p);
+void lcConv2dIoPolicyDefault(lcConv2dIoPolicy* p);
+void lcVectorAddIoPolicyDefault(lcVectorAddIoPolicy* p);
+
+/* Resident-loop presets, include/lightning_core/core/ops/policy.hpp:37-71
+ * (start: upload, no download, no sync; run: nothing; finish: download+sync; sync: sync). */
+typedef enum lcLoopStage { LC_LOOP_START = 0, LC_LOOP_RUN, LC_LOOP_FINISH, LC_LOOP_SYNC } lcLoopStage;
+void lcMatMulPolicyForStage(lcLoopStage stage, lcMatMulIoPolicy* p);
+
+/* Attention forward over `units` independent heads laid out [units, seq, head_dim].
+ * Replaces attentionForwardWithPolicy (src/attention.cpp:137-201) for Device::kCUDA, batched.
+ * scale = 1/sqrt(head_dim); causal masks j > i. f32: strict fp32, any head_dim <= 256.
+ * bf16: tcgen05 flash attention for head_dim 64/128 (others: fp32-math SIMT kernel). */
+lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* out, size_t units, size_t seq,
+                             size_t head_dim, int causal, lcDataType dtype, const lcAttentionIoPolicy* policy,
+                             lcStream_t stream);
+
+/* C[m,n] = A[m,k] B[k,n], row-major, no transposes; replaces ops::matMulWithPolicy<T>
+ * (include/lightning_core/core/ops.hpp:354-459) for Device::kCUDA.  bf16: tcgen05 GEMM with
+ * fp32 accumulation (needs k%8==0 and n%8==0, else a SIMT kernel). f32: strict fp32. */
+lcError_t lcMatMul(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
+                   const lcMatMulIoPolicy* policy, lcStream_t stream);
+
+/* NCHW x OIHW (+bias, may be NULL) -> NCHW, optional ReLU; replaces ops::conv2dNchw<float>
+ * (include/lightning_core/core/ops.hpp:855-1212).  fp32 strict implicit GEMM. */
+lcError_t lcConv2dNchw(const float* x, const float* w, const float* bias, float* out, size_t batch,
+                       size_t in_channels, size_t in_h, size_t in_w, size_t out_channels, size_t kernel_h,
+                       size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w,
+                       int apply_relu, const lcConv2dIoPolicy* policy, lcStream_t stream);
+
+/* Integrated conv2d+ReLU -> QKV arrange -> non-causal attention -> optional projection.
+ * Replaces convAttentionTorchstrongNchwIntoDirect (python/bindings/bind_integrated.cpp:614-730)
+ * plus the attention_qkv_proj pattern (include/lightning_core/core/graph.hpp:3529-3547).
+ *   per_image = 0: the reference's semantics for any batch: one attention over the first
+ *                  3*seq*head_dim floats of the flat conv output (cyclically repeated if short);
+ *                  out is [seq, cols].
+ *   per_image = 1: image b runs those batch-1 semantics on x[b]; out is [batch, seq, cols].
+ * cols = proj_cols when proj_w ([head_dim, proj_cols]) is given, else head_dim.
+ * Policy flags refer to x/w/bias/proj_w (upload_x .. upload_bias; proj_w follows upload_w). */
+lcError_t lcConvAttentionNchw(const float* x, const float* w, const float* bias, const float* proj_w, float* out,
+                              size_t batch, size_t in_channels, size_t in_h, size_t in_w, size_t out_channels,
+                              size_t kernel_h, size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h,
+                              size_t pad_w, size_t seq, size_t head_dim, size_t proj_cols, int per_image,
+                              const lcConv2dIoPolicy* policy, lcStream_t stream);
+
+/* out = a + b (f32 or f64); replaces vectorAddCuda (src/ops/vector_add_cuda.cu:12-86). */
+lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataType dtype,
+                      const lcVectorAddIoPolicy* policy, lcStream_t stream);
+
+/* (x - mean)/sqrt(var + eps) over the last axis, population variance, no affine
+ * (the reference's LN formula, README.md:2267-2270).  Device pointers, fp32. */
+lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, float eps, lcStream_t stream);
+
+/* ---- device error word: kernels' bounded waits record where they gave up ---------------- */
+/* Returns LC_DRIVER_ERROR and the recorded code if any kernel on the current device gave up a
+ * bounded wait since the last clear; LC_SUCCESS otherwise.  Synchronizes the device. */
+lcError_t lcGetDeviceErrorWord(unsigned int* code);
+lcError_t lcClearDeviceErrorWord(void);
+
+/* ---- runtime trace ring (src/runtime.cpp:63-99,620-760) ---------------------------------- */
+typedef struct lcRuntimeTraceEvent {
+  int type;   /* RuntimeTraceEventType: 0 malloc .. 10 op_dispatch          */
+  int status; /* lcError_t                                                   */
+  uint64_t timestamp_ns;
+  size_t size_bytes;
+  int detail0; /* op kind for op_dispatch (1 matmul .. 6 attention_forward)  */
+  int detail1; /* requested | selected<<4 | fallback<<8                      */
+} lcRuntimeTraceEvent;
+void lcRuntimeTraceSetEnabled(int enabled);
+int lcRuntimeTraceIsEnabled(void);
+void lcRuntimeTraceClear(void);
+size_t lcRuntimeTraceCount(void);
+size_t lcRuntimeTraceCapacity(void);
+lcError_t lcRuntimeTraceGet(size_t index, lcRuntimeTraceEvent* out_event);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LC_B200_H */
