@@ -1,0 +1,420 @@
+"""Benchmark of the attention + matmul2d hot path on B200 (one process per GPU).
+
+Metric: "attention & matmul2d TFLOP/s (% of B200 peak)".  One step = the two BASELINE configs
+the north star targets, sharded across the N ranks with no data-path collective:
+  * config 3: causal bf16 attention, Q/K/V [B=8, H=16, S=2048, D=128] -> 128 (b,h) units,
+    units/N per rank; algorithmic FLOPs 4*S^2*D/2 per unit (causal half) = 1.074 GFLOP.
+  * config 4: bf16 GEMM 8192^3 (fp32 accumulate, bf16 out) -> A row-blocks of 8192/N rows per
+    rank, B replicated; FLOPs 2*M*N*K = 1.0995 TFLOP in total.
+value = total algorithmic FLOPs of the step / step time (max over ranks), TFLOP/s, strong
+scaling (the total work is the config; ranks split it).  The assembling all-gather of the
+outputs (NCCL over NVLink) is timed separately and reported as `assemble_ms`.
+
+Inputs are synthetic (seeded normal / uniform as BASELINE.json describes), larger than L2 for the
+GEMM; L2 is flushed (a 256 MiB write) between timed steps.  Kernel times are CUDA events on the
+launching stream.  `e2e` runs the same step through the C ABI with host (pinned) buffers and the
+reference's default IO policy (upload, download, synchronize), copies included.
+
+--impl reference times the reference's own CPU implementation (oracle/_ref, built from the
+reference sources) on a bounded sample of the same workload on the host cores.
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "lightining-core_b200", "python"))
+
+B, H, S, D = 8, 16, 2048, 128
+UNITS = B * H
+GM = GN = GK = 8192
+ATTN_FLOPS_PER_UNIT = 4.0 * S * S * D / 2.0  # causal: half the S x S tile work (FA convention)
+GEMM_FLOPS = 2.0 * GM * GN * GK
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name> ('traffic_bytes_per_launch:')."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (the profiling recipe's clocks line)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"lc_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ----------------------------------------------------------------------------- reference arm
+def cpu_sample(threads, heads=32, rows=256):
+    """Reference CPU path on a bounded sample of the workload: `heads` causal attention units and
+    `rows` rows of the 8192^3 GEMM.  Returns (TFLOP/s, seconds, sample description)."""
+    from oracle import oracle as O
+
+    kind = "reference" if O.ref_available() else "port"
+    L = O.ref() if kind == "reference" else O.port()
+    rng = np.random.default_rng(2)
+    bfr = O.port().bf16_round
+    q, k, v = (bfr(rng.standard_normal((heads, S, D), dtype=np.float32)) for _ in range(3))
+    a = bfr((rng.uniform(-1, 1, (rows, GK)) / np.sqrt(GK)).astype(np.float32))
+    bm = bfr((rng.uniform(-1, 1, (GK, GN)) / np.sqrt(GK)).astype(np.float32))
+    t0 = time.perf_counter()
+    L.attention_units(q, k, v, causal=True, threads=threads)
+    t1 = time.perf_counter()
+    L.matmul(a, bm, threads=threads)
+    t2 = time.perf_counter()
+    flops = heads * ATTN_FLOPS_PER_UNIT + 2.0 * rows * GN * GK
+    desc = (f"{heads} of 128 causal heads [2048,128] + {rows} of 8192 GEMM rows (8192x8192), bf16-rounded "
+            f"inputs widened to fp32; attention {t1 - t0:.2f}s, gemm {t2 - t1:.2f}s on {threads} threads")
+    return flops / (t2 - t0) / 1e12, t2 - t0, desc, kind
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, secs, desc, kind = cpu_sample(threads)
+        if i >= args.warmup:
+            vals.append((v, secs))
+    val = float(np.median([x[0] for x in vals]))
+    ms = float(np.median([x[1] for x in vals])) * 1e3
+    line = {"metric": "attention & matmul2d TFLOP/s (% of B200 peak)", "value": val, "unit": "TFLOP/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": dict(CONFIG, parallelism=f"cpu threads x{threads} (bounded sample of the workload)"),
+            "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": desc},
+            "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+CONFIG = {"workload": "cfg3 causal attention bf16 [8,16,2048,128] + cfg4 matmul2d bf16 8192^3 (fp32 accumulate)",
+          "attention": "B=8 H=16 S=2048 D=128 causal, N(0,1) bf16, scale 1/sqrt(128)",
+          "gemm": "M=N=K=8192, U(-1,1)/sqrt(K) bf16, row-major, bf16 out",
+          "l2": "flushed between timed steps (256 MiB write); GEMM inputs 268 MB > L2"}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    import lightning_core_b200 as lc
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    L = lc.lib
+
+    # ---- shards: units [u0, u1) of attention, rows [r0, r1) of the GEMM
+    per_u = UNITS // world
+    u0, u1 = rank * per_u, (rank + 1) * per_u
+    per_r = GM // world
+    r0, r1 = rank * per_r, (rank + 1) * per_r
+    nu, nr = u1 - u0, r1 - r0
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    qkv = torch.randn((3, UNITS, S, D), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    q, k, v = (qkv[i, u0:u1].contiguous() for i in range(3))
+    del qkv
+    attn_out = torch.empty_like(q)
+    g.manual_seed(3)
+    A = ((torch.rand((GM, GK), generator=g, device=dev) * 2 - 1) / GK ** 0.5).to(torch.bfloat16)[r0:r1].contiguous()
+    Bm = ((torch.rand((GK, GN), generator=g, device=dev) * 2 - 1) / GK ** 0.5).to(torch.bfloat16)
+    Cm = torch.empty((nr, GN), device=dev, dtype=torch.bfloat16)
+    flush = torch.empty(256 << 20, device=dev, dtype=torch.uint8)
+    torch.cuda.synchronize()
+
+    def attn():
+        lc.check(L.lcAttentionForward(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                                      C.c_void_p(attn_out.data_ptr()), nu, S, D, 1, lc.BF16, None, sp), "attention")
+
+    def gemm():
+        lc.check(L.lcMatMul(C.c_void_p(A.data_ptr()), C.c_void_p(Bm.data_ptr()), C.c_void_p(Cm.data_ptr()), nr, GK,
+                            GN, lc.BF16, None, sp), "matmul")
+
+    for _ in range(args.warmup):
+        attn()
+        gemm()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with Clocks(local_rank) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        for i in range(args.steps):
+            flush.zero_()
+            ev[i][0].record(stream)
+            attn()
+            ev[i][1].record(stream)
+            gemm()
+            ev[i][2].record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    attn_ms = [e[0].elapsed_time(e[1]) for e in ev]
+    gemm_ms = [e[1].elapsed_time(e[2]) for e in ev]
+    step_ms = sum(a + b for a, b in zip(attn_ms, gemm_ms)) / args.steps
+    t = torch.tensor([step_ms, float(np.mean(attn_ms)), float(np.mean(gemm_ms))], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    step_ms, attn_avg, gemm_avg = (float(x) for x in t.tolist())
+    total_flops = UNITS * ATTN_FLOPS_PER_UNIT + GEMM_FLOPS
+    value = total_flops / (step_ms * 1e-3) / 1e12
+
+    # ---- assembling all-gather (outside the compute timing)
+    assemble_ms = None
+    if world > 1:
+        full_attn = torch.empty((world * nu, S, D), device=dev, dtype=torch.bfloat16)
+        full_c = torch.empty((world * nr, GN), device=dev, dtype=torch.bfloat16)
+        for _ in range(2):
+            dist.all_gather_into_tensor(full_attn, attn_out)
+            dist.all_gather_into_tensor(full_c, Cm)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dist.all_gather_into_tensor(full_attn, attn_out)
+        dist.all_gather_into_tensor(full_c, Cm)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        am = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        dist.all_reduce(am, op=dist.ReduceOp.MAX)
+        assemble_ms = float(am.item())
+        del full_attn, full_c
+
+    # ---- e2e through the C ABI with host buffers and the reference's default policy
+    e2e = e2e_run(args, lc, torch, q, k, v, A, Bm, nu, nr, world, dev)
+
+    # ---- extra configs (N=1 only): fp32 attention [256,64], fp32 matmul 1024^3, conv->attention pipeline
+    extras = extra_configs(args, lc, torch, dev, sp) if world == 1 else None
+
+    if rank != 0:
+        return
+    pk, pk_kind = peaks()
+    peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    gemm_ach = 2.0 * nr * GN * GK / (gemm_avg * 1e-3) / 1e12
+    attn_ach = nu * ATTN_FLOPS_PER_UNIT / (attn_avg * 1e-3) / 1e12
+    traffic = profile_traffic("gemm_bf16_8192.md")
+    cpu = None
+    if world == 1:
+        cv, secs, desc, kind = cpu_sample(os.cpu_count() or 1)
+        cpu = {"value": cv, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": kind, "sample": desc}
+    line = {
+        "metric": "attention & matmul2d TFLOP/s (% of B200 peak)", "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"shard x{world}: attention units/{world}, gemm rows/{world}"),
+        "frac_of_peak": value / peak, "peak_tflops": peak, "peak_kind": pk_kind,
+        "parts": {"attention_ms": attn_avg, "attention_tflops": attn_ach, "attention_frac": attn_ach / peak,
+                  "gemm_ms": gemm_avg, "gemm_tflops": gemm_ach, "gemm_frac": gemm_ach / peak},
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel", "achieved": gemm_ach, "peak": peak,
+                     "unit": "TFLOP/s", "frac": gemm_ach / peak,
+                     "peak_source": f"{pk_kind} bf16_tflops (burst; kernel timed alone)",
+                     "traffic": None if traffic is None else traffic * nr / GM},
+        "assemble_ms": assemble_ms,
+        "e2e": e2e,
+        "gpu_launches": 2 * args.steps * world,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "extras": extras,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def e2e_run(args, lc, torch, q, k, v, A, Bm, nu, nr, world, dev):
+    """Same step through the public C ABI with pinned host buffers: the reference's default IO
+    policy (upload inputs, download output, synchronize) on each call, copies inside the timing."""
+    import torch.distributed as dist
+
+    L = lc.lib
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    ha, hb = A.cpu().pin_memory(), Bm.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+    hc = torch.empty((nr, GN), dtype=torch.bfloat16).pin_memory()
+    apol = lc.default_attention_policy()
+    mpol = lc.default_matmul_policy()
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+
+    def step():
+        lc.check(L.lcAttentionForward(ptr(hq), ptr(hk), ptr(hv), ptr(ho), nu, S, D, 1, lc.BF16, C.byref(apol), None),
+                 "attention e2e")
+        lc.check(L.lcMatMul(ptr(ha), ptr(hb), ptr(hc), nr, GK, GN, lc.BF16, C.byref(mpol), None), "matmul e2e")
+
+    steps = max(2, min(args.steps, 5))
+    for _ in range(2):
+        step()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    t = torch.tensor([dt], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    h2d = (hq.numel() * 3 + ha.numel() + hb.numel()) * 2
+    d2h = (ho.numel() + hc.numel()) * 2
+    total_flops = UNITS * ATTN_FLOPS_PER_UNIT + GEMM_FLOPS
+    return {"value": total_flops / dt / 1e12, "unit": "TFLOP/s", "ms_per_step": dt * 1e3,
+            "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+            "timing": "wall clock around synchronous C-ABI calls, max over ranks", "steps": steps}
+
+
+def extra_configs(args, lc, torch, dev, sp):
+    """The fp32 configs at N=1: attention [256,64] (cfg 1), matmul 1024^3 (cfg 2), the integrated
+    conv->attention->projection pipeline [32,64,56,56] (cfg 5).  Device pointers, CUDA events."""
+    L = lc.lib
+    stream = torch.cuda.current_stream()
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    g = torch.Generator(device=dev)
+    res = {}
+
+    def timeit(fn, reps):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    g.manual_seed(0)
+    q, k, v = (torch.randn((256, 64), generator=g, device=dev) for _ in range(3))
+    o = torch.empty_like(q)
+    ms = timeit(lambda: lc.check(L.lcAttentionForward(ptr(q), ptr(k), ptr(v), ptr(o), 1, 256, 64, 0, lc.F32, None,
+                                                      sp)), 50)
+    res["cfg1_attention_f32_256x64"] = {"ms": ms, "tflops": 4 * 256 * 256 * 64 / (ms * 1e-3) / 1e12}
+    for n in (256, 512, 1024, 2048):
+        g.manual_seed(1)
+        a = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        b = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        c = torch.empty_like(a)
+        ms = timeit(lambda: lc.check(L.lcMatMul(ptr(a), ptr(b), ptr(c), n, n, n, lc.F32, None, sp)), 10)
+        res[f"cfg2_matmul_f32_{n}"] = {"ms": ms, "tflops": 2 * n ** 3 / (ms * 1e-3) / 1e12}
+    g.manual_seed(4)
+    x = torch.randn((32, 64, 56, 56), generator=g, device=dev)
+    bound = (6 / 576) ** 0.5
+    w = (torch.rand((192, 64, 3, 3), generator=g, device=dev) * 2 - 1) * bound
+    bias = torch.zeros(192, device=dev)
+    g.manual_seed(5)
+    pw = (torch.rand((64, 64), generator=g, device=dev) * 2 - 1) * (6 / 64) ** 0.5
+    out = torch.empty((32, 3136, 64), device=dev)
+    ms = timeit(lambda: lc.check(L.lcConvAttentionNchw(ptr(x), ptr(w), ptr(bias), ptr(pw), ptr(out), 32, 64, 56, 56,
+                                                       192, 3, 3, 1, 1, 1, 1, 3136, 64, 64, 1, None, sp)), 3)
+    flops = 2 * 32 * 3136 * 192 * 576 + 32 * 4 * 3136 ** 2 * 64 + 2 * 32 * 3136 * 64 * 64
+    res["cfg5_conv_attention_f32"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    try:
+        run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

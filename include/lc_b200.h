@@ -34,6 +34,9 @@
 #ifdef __cplusplus
 extern "C" {
 #endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
 
 /* ===================== Part 1: reference runtime ABI (lightning_core.h) ================= */
 
@@ -253,6 +256,9 @@ size_t lcRuntimeTraceCount(void);
 size_t lcRuntimeTraceCapacity(void);
 lcError_t lcRuntimeTraceGet(size_t index, lcRuntimeTraceEvent* out_event);
 
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
 #ifdef __cplusplus
 }
 #endif

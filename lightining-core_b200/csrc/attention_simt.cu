@@ -1,0 +1,250 @@
+// Flash-style attention forward on CUDA cores, strict fp32 arithmetic.
+//
+// Restates src/attention_cpu.cpp:38-101 of the reference without the S x S buffers: per query
+// row, scores s_j = (q_i . k_j) * (1/sqrt(d)) with j > i masked when causal, softmax with the
+// running row maximum, and out_i = sum_j p_j v_j -- computed tile by tile with the usual
+// online-softmax rescaling, so memory is O(S) and nothing but Q, K, V and O touches HBM.
+// The postprocess of src/attention.cpp:41-60 (out*scale + bias, optional ReLU) and, for the
+// integrated conv->attention pipeline, the projection attn_out[S, d] @ W[d, P]
+// (include/lightning_core/core/graph.hpp:3529-3547) run in the epilogue.
+//
+// This is the kernel for the fp32 contract (|err| <= 1e-4 + 1e-4|ref|), which plain TF32 tensor
+// cores cannot meet, and the fallback for bf16 head dims the tcgen05 kernel does not take.
+//
+// CTA = 256 threads, 64 query rows x 64-key tiles.  Thread t owns rows (t>>4)*4 .. +3; its 16
+// lanes t&15 of that row group split the 64 score columns (4 each) and the output columns, so
+// row max / sum reductions are 4 xor-shuffles inside a half warp.  Q^T and K^T are staged
+// transposed so every shared-memory read in the two inner products is a float4.
+#include <cuda_bf16.h>
+#include <math.h>
+
+#include "lc_internal.hpp"
+
+namespace lcb {
+namespace {
+
+constexpr int TQ = 64, TK = 64, NT = 256;
+
+template <typename T>
+__device__ __forceinline__ float ld_f(const T* p) { return static_cast<float>(*p); }
+template <>
+__device__ __forceinline__ float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <typename T>
+__device__ __forceinline__ void st_f(T* p, float v) { *p = static_cast<T>(v); }
+template <>
+__device__ __forceinline__ void st_f<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+// DP: padded head dim (64, 128 or 256); columns >= d are zero in Q/K/V staging.
+template <int DP, typename T>
+__global__ void __launch_bounds__(NT) attn_simt_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  float* Qt = smem;              // [DP][TQ]
+  float* Kt = Qt + DP * TQ;      // [DP][TK]
+  float* Vs = Kt + DP * TK;      // [TK][DP]
+  float* Pt = Vs + TK * DP;      // [TK][TQ]
+  float* Ws = Pt + TK * TQ;      // [d][P] (projection only)
+
+  const int tid = threadIdx.x;
+  const int rg = tid >> 4, cg = tid & 15;
+  const int unit = blockIdx.y;
+  const int q0 = blockIdx.x * TQ;
+  const int S = a.seq, D = a.d;
+  const T* q = static_cast<const T*>(a.q) + unit * a.q_unit_stride;
+  const T* k = static_cast<const T*>(a.k) + unit * a.k_unit_stride;
+  const T* v = static_cast<const T*>(a.v) + unit * a.v_unit_stride;
+
+  // Stage Q^T: element (r, c) -> Qt[c][r]; r fastest across threads (conflict-free stores).
+  for (int idx = tid; idx < TQ * DP; idx += NT) {
+    const int r = idx % TQ, c = idx / TQ;
+    const int gr = q0 + r;
+    Qt[c * TQ + r] = (gr < S && c < D) ? ld_f(q + static_cast<long long>(gr) * D + c) : 0.0f;
+  }
+
+  constexpr int DC = DP / 16;  // output columns per thread: (g*16 + cg)*4 + e, g < DP/64
+  float o[4][DC];
+  float m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < DC; ++j) o[i][j] = 0.0f;
+  }
+
+  int kv_end = S;
+  if (a.causal) kv_end = min(S, q0 + TQ);
+  const int ntiles = (kv_end + TK - 1) / TK;
+  for (int t = 0; t < ntiles; ++t) {
+    const int k0 = t * TK;
+    __syncthreads();  // previous tile's Kt/Vs/Pt fully consumed
+    for (int idx = tid; idx < TK * DP; idx += NT) {
+      const int j = idx % TK, c = idx / TK;
+      const int gj = k0 + j;
+      Kt[c * TK + j] = (gj < S && c < D) ? ld_f(k + static_cast<long long>(gj) * D + c) : 0.0f;
+    }
+    for (int idx = tid; idx < TK * DP; idx += NT) {
+      const int c = idx % DP, j = idx / DP;
+      const int gj = k0 + j;
+      Vs[j * DP + c] = (gj < S && c < D) ? ld_f(v + static_cast<long long>(gj) * D + c) : 0.0f;
+    }
+    __syncthreads();
+
+    float s[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[i][j] = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < DP; ++c) {
+      const float4 qa = *reinterpret_cast<const float4*>(Qt + c * TQ + rg * 4);
+      const float4 kb = *reinterpret_cast<const float4*>(Kt + c * TK + cg * 4);
+      const float qv[4] = {qa.x, qa.y, qa.z, qa.w};
+      const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s[i][j] = fmaf(qv[i], kv[j], s[i][j]);
+    }
+
+    // Scale, mask, online softmax (row statistics over the 16 lanes of this row group).
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gi = q0 + rg * 4 + i;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int gj = k0 + cg * 4 + j;
+        float x = s[i][j] * a.scale;
+        if (gj >= S || (a.causal && gj > gi)) x = -INFINITY;
+        s[i][j] = x;
+        mx = fmaxf(mx, x);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m[i], mx);
+      // A fully masked row so far keeps m = -inf; use 0 as the reference point then.
+      const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
+      const float corr = expf(m[i] - m_use);
+      float sum = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = expf(s[i][j] - m_use);
+        s[i][j] = p;
+        sum += p;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      l[i] = l[i] * corr + sum;
+      m[i] = m_new;
+#pragma unroll
+      for (int j = 0; j < DC; ++j) o[i][j] *= corr;
+    }
+    // P^T to shared memory: Pt[j][row].
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(Pt + (cg * 4 + j) * TQ + rg * 4) = make_float4(s[0][j], s[1][j], s[2][j], s[3][j]);
+    __syncthreads();
+
+    const int jmax = min(TK, kv_end - k0);
+#pragma unroll 4
+    for (int j = 0; j < jmax; ++j) {
+      const float4 pa = *reinterpret_cast<const float4*>(Pt + j * TQ + rg * 4);
+      const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
+#pragma unroll
+      for (int g = 0; g < DP / 64; ++g) {
+        const float4 vb = *reinterpret_cast<const float4*>(Vs + j * DP + (g * 16 + cg) * 4);
+        const float vv[4] = {vb.x, vb.y, vb.z, vb.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[i][g * 4 + e] = fmaf(pv[i], vv[e], o[i][g * 4 + e]);
+      }
+    }
+  }
+
+  // Normalise, postprocess.
+  const bool post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float inv = 1.0f / l[i];
+#pragma unroll
+    for (int j = 0; j < DC; ++j) {
+      float x = o[i][j] * inv;
+      if (post) {
+        x = x * a.post_scale + a.post_bias;
+        if (a.post_relu && x < 0.0f) x = 0.0f;
+      }
+      o[i][j] = x;
+    }
+  }
+
+  if (a.proj_w == nullptr) {
+    T* out = static_cast<T*>(a.out) + unit * a.out_unit_stride;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gi = q0 + rg * 4 + i;
+      if (gi >= S) continue;
+#pragma unroll
+      for (int g = 0; g < DP / 64; ++g)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = (g * 16 + cg) * 4 + e;
+          if (c < D) st_f(out + static_cast<long long>(gi) * D + c, o[i][g * 4 + e]);
+        }
+    }
+    return;
+  }
+
+  // Fused projection: out[i, :] = attn[i, :] @ W, sequential over the d inner index.
+  const int P = a.proj_cols;
+  __syncthreads();
+  float* Os = Qt;  // reuse: [TQ][DP]
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int g = 0; g < DP / 64; ++g)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) Os[(rg * 4 + i) * DP + (g * 16 + cg) * 4 + e] = o[i][g * 4 + e];
+  for (int idx = tid; idx < D * P; idx += NT) Ws[idx] = __ldg(a.proj_w + idx);
+  __syncthreads();
+  float* out = static_cast<float*>(a.out) + unit * a.out_unit_stride;
+  for (int col = cg; col < P; col += 16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = rg * 4 + i;
+      float acc = 0.0f;
+      for (int c = 0; c < D; ++c) acc = fmaf(Os[r * DP + c], Ws[c * P + col], acc);
+      const int gi = q0 + r;
+      if (gi < S) out[static_cast<long long>(gi) * P + col] = acc;
+    }
+  }
+}
+
+template <int DP, typename T>
+cudaError_t launch(const AttnArgs& a, cudaStream_t s) {
+  size_t smem = sizeof(float) * (3 * DP * 64 + 64 * 64);
+  if (a.proj_w) smem += sizeof(float) * a.d * a.proj_cols;
+  cudaError_t e = cudaFuncSetAttribute(attn_simt_kernel<DP, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid((a.seq + TQ - 1) / TQ, a.units);
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  attn_simt_kernel<DP, T><<<grid, NT, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t dispatch(const AttnArgs& a, cudaStream_t s) {
+  if (a.proj_w && (a.d > 128 || a.proj_cols > 128 || sizeof(T) != 4)) return cudaErrorNotSupported;
+  if (a.d <= 64) return launch<64, T>(a, s);
+  if (a.d <= 128) return launch<128, T>(a, s);
+  if (a.d <= 256) return launch<256, T>(a, s);
+  return cudaErrorNotSupported;
+}
+
+}  // namespace
+
+cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s) { return dispatch<float>(a, s); }
+cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s) { return dispatch<__nv_bfloat16>(a, s); }
+
+}  // namespace lcb

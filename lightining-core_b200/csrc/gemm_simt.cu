@@ -1,0 +1,206 @@
+// Strict-fp32 SIMT GEMM and implicit-GEMM conv for sm_100a.
+//
+// The reference's fp32 contract (src/ops/matmul_cpu.cpp:49-60, max abs/rel error 1e-4 against
+// it) rules out plain TF32 tensor cores, so these kernels accumulate with fp32 FFMA in k order,
+// exactly the reduction order of the reference's i-p-j loop for each output element.
+//
+// Tiling: 128x128 output tile per 256-thread CTA, BK = 8, double-buffered shared memory, each
+// thread owns an 8x8 sub-tile split into two 4-row x two 4-column strips (rows ty*4 and
+// ty*4+64, cols tx*4 and tx*4+64) so the float4 shared-memory reads are conflict-free.
+// The operands come from loader functors: dense row-major for matmul, an on-the-fly im2col
+// gather (B side) for conv (the im2col matrix is never materialised); the epilogue functor writes
+// row-major for matmul or NCHW (+bias, ReLU) for conv.
+#include <cuda_bf16.h>
+
+#include "lc_internal.hpp"
+
+namespace lcb {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 8, NT = 256;
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v) { return static_cast<float>(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// Dense row-major A[m,k].
+template <typename T>
+struct DenseA {
+  const T* a;
+  int m, k;
+  __device__ __forceinline__ float operator()(int r, int c) const {
+    return (r < m && c < k) ? to_f(a[static_cast<long long>(r) * k + c]) : 0.0f;
+  }
+};
+// Dense row-major B[k,n].
+template <typename T>
+struct DenseB {
+  const T* b;
+  int k, n;
+  __device__ __forceinline__ float operator()(int r, int c) const {
+    return (r < k && c < n) ? to_f(b[static_cast<long long>(r) * n + c]) : 0.0f;
+  }
+};
+// Transposed im2col view of NCHW x: B[k = (c, ky, kx), col = (img, oy, ox)].  The k order is
+// the reference's im2col column order (include/lightning_core/core/ops.hpp:1082-1084);
+// out-of-image taps read as zero.  Conv runs as out^T[oc, pix] = W[oc, k] * im2col^T[k, pix] so
+// that consecutive threads own consecutive pixels and the NCHW stores coalesce.
+struct Im2colB {
+  const float* x;
+  int cols, kdim, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow;
+  __device__ __forceinline__ float operator()(int c, int r) const {
+    if (r >= cols || c >= kdim) return 0.0f;
+    const int hw = oh * ow;
+    const int img = r / hw, pix = r - img * hw;
+    const int oy = pix / ow, ox = pix - oy * ow;
+    const int khw = kh * kw;
+    const int ch = c / khw, rem = c - ch * khw;
+    const int ky = rem / kw, kx = rem - ky * kw;
+    const int y = oy * sh + ky - ph, xx = ox * sw + kx - pw;
+    if (y < 0 || y >= in_h || xx < 0 || xx >= in_w) return 0.0f;
+    return __ldg(x + ((static_cast<long long>(img) * in_c + ch) * in_h + y) * in_w + xx);
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void store_val(T* p, float v) { *p = static_cast<T>(v); }
+template <>
+__device__ __forceinline__ void store_val<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <typename T>
+struct RowMajorEpi {
+  T* c;
+  int m, n;
+  __device__ __forceinline__ void operator()(int r, int col, float v) const {
+    if (r < m && col < n) store_val(c + static_cast<long long>(r) * n + col, v);
+  }
+};
+// NCHW store of out^T[oc, pix] with bias + optional ReLU (ops.hpp:1196-1210).
+struct NchwEpi {
+  float* out;
+  const float* bias;
+  int rows, out_c, hw, relu;
+  __device__ __forceinline__ void operator()(int oc, int r, float v) const {
+    if (r >= rows || oc >= out_c) return;
+    v += bias ? __ldg(bias + oc) : 0.0f;
+    if (relu && v < 0.0f) v = 0.0f;
+    const int img = r / hw, pix = r - img * hw;
+    out[(static_cast<long long>(img) * out_c + oc) * hw + pix] = v;
+  }
+};
+
+template <class LA, class LB, class Epi>
+__global__ void __launch_bounds__(NT) simt_gemm_kernel(LA la, LB lb, Epi epi, int M, int N, int K) {
+  __shared__ __align__(16) float As[2][BK][BM];
+  __shared__ __align__(16) float Bs[2][BK][BN];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int row0 = blockIdx.y * BM, col0 = blockIdx.x * BN;
+
+  // Loader assignment: A tile 128x8 -> thread loads row (tid>>1), k (tid&1)*4 .. +3.
+  const int a_r = tid >> 1, a_k = (tid & 1) * 4;
+  // B tile 8x128 -> thread loads k (tid>>5), cols (tid&31)*4 .. +3.
+  const int b_k = tid >> 5, b_c = (tid & 31) * 4;
+
+  float ra[4], rb[4];
+  auto gload = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ra[i] = la(row0 + a_r, k0 + a_k + i);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) rb[i] = lb(k0 + b_k, col0 + b_c + i);
+  };
+  auto sstore = [&](int buf) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) As[buf][a_k + i][a_r] = ra[i];
+    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_c]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+  };
+
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+  const int ktiles = (K + BK - 1) / BK;
+  gload(0);
+  sstore(0);
+  __syncthreads();
+  for (int kt = 0; kt < ktiles; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < ktiles) gload((kt + 1) * BK);
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + 64]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + 64]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (kt + 1 < ktiles) {
+      sstore(buf ^ 1);
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = row0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = col0 + tx * 4 + (j & 3) + (j >> 2) * 64;
+      epi(r, c, acc[i][j]);
+    }
+  }
+}
+
+template <class LA, class LB, class Epi>
+cudaError_t run(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s) {
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  simt_gemm_kernel<<<grid, NT, 0, s>>>(la, lb, epi, M, N, K);
+  return cudaGetLastError();
+}
+
+__global__ void repeat_fill_kernel(const float* src, size_t have, float* dst, size_t total) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i % have];
+}
+
+}  // namespace
+
+cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
+  return run(DenseA<float>{a, m, k}, DenseB<float>{b, k, n}, RowMajorEpi<float>{c, m, n}, m, n, k, s);
+}
+
+cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                           cudaStream_t s) {
+  return run(DenseA<__nv_bfloat16>{a, m, k}, DenseB<__nv_bfloat16>{b, k, n}, RowMajorEpi<__nv_bfloat16>{c, m, n}, m,
+             n, k, s);
+}
+
+cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
+                            cudaStream_t s) {
+  const int oh = (in_h + 2 * ph - kh) / sh + 1;
+  const int ow = (in_w + 2 * pw - kw) / sw + 1;
+  const int rows = batch * oh * ow;
+  const int kdim = in_c * kh * kw;
+  DenseA<float> la{w, out_c, kdim};  // OIHW is already W[oc, k] row-major
+  Im2colB lb{x, rows, kdim, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow};
+  NchwEpi epi{out, bias, rows, out_c, oh * ow, relu};
+  return run(la, lb, epi, out_c, rows, kdim, s);
+}
+
+cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s) {
+  if (have == 0) return cudaErrorInvalidValue;
+  repeat_fill_kernel<<<592, 256, 0, s>>>(src, have, dst, total);
+  return cudaGetLastError();
+}
+
+}  // namespace lcb

@@ -1,0 +1,328 @@
+// bf16 GEMM on the 5th-generation tensor cores: C[M,N] (bf16) = A[M,K] (bf16) * B[K,N] (bf16),
+// fp32 accumulation in TMEM.  Replaces the matmul2d hot loop (reference: ops::matMulWithPolicy,
+// include/lightning_core/core/ops.hpp:354-459; CPU loop src/ops/matmul_cpu.cpp:49-60) for the
+// bf16 configs.  Both operands keep the reference's row-major layout: A is K-major, B is
+// N-major ("MN-major" in UMMA terms), so no transpose pass ever runs.
+//
+// Structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile 128x64 (one 16 KB box) + B tile 64x256 (four 8 KB boxes of
+//               64 N-columns), 128-byte swizzle, 4-stage mbarrier ring.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16) x 4 per stage,
+//               commits the stage back to the producer, and commits a finished accumulator to
+//               the epilogue.  Accumulators are double-buffered in TMEM (2 x 256 columns) so
+//               the next tile's MMAs overlap the previous tile's epilogue.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (each warp owns the TMEM lane
+//               quarter warp%4), convert to bf16, store.
+// Tiles are walked in groups of 16 M-blocks so the A and B panels in flight stay in L2.
+// Every mbarrier wait is bounded (common.cuh); on a timeout the CTA drains and exits.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "lc_internal.hpp"
+
+namespace lcb {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int NUM_THREADS = 192;
+constexpr int A_STAGE_BYTES = BM * BK * 2;          // 16 KB
+constexpr int B_CHUNK_BYTES = BK * 64 * 2;          // 8 KB: 64 K-rows x 64 N-cols
+constexpr int B_STAGE_BYTES = BK * BN * 2;          // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 512;                      // 2 accumulators x 256 fp32 columns
+constexpr int GROUP_M = 16;
+constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, /*a_mn_major=*/0, /*b_mn_major=*/1);
+
+struct SharedTail {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[2];
+  uint64_t tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + sizeof(SharedTail);
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int group = GROUP_M * tiles_n;
+  const int g = t / group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(GROUP_M, tiles_m - first_m);
+  const int r = t - g * group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                        __nv_bfloat16* __restrict__ C, int M, int N, int K, unsigned* err_word) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * A_STAGE_BYTES;
+  SharedTail* st = reinterpret_cast<SharedTail*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&st->tmem_full[b], 1);
+      mbar_init(&st->tmem_empty[b], 4);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 0) {
+    tmem_alloc(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int inflight_stage[STAGES];
+      uint32_t inflight_phase[STAGES];
+      int ninflight = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&st->full[stage], STAGE_BYTES);
+          tma_load_2d(smem_a + stage * A_STAGE_BYTES, &map_a, kb * BK, mb * BM, &st->full[stage]);
+          uint8_t* bdst = smem_b + stage * B_STAGE_BYTES;
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c)
+            tma_load_2d(bdst + c * B_CHUNK_BYTES, &map_b, nb * BN + c * 64, kb * BK, &st->full[stage]);
+          inflight_stage[ninflight % STAGES] = stage;
+          inflight_phase[ninflight % STAGES] = phase;
+          ++ninflight;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Abort path: let the copies already issued land before the CTA's shared memory goes away.
+        const int n = ninflight < STAGES ? ninflight : STAGES;
+        for (int i = 0; i < n; ++i) {
+          const int idx = (ninflight - 1 - i) % STAGES;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&st->full[inflight_stage[idx]], inflight_phase[idx]) &&
+                 globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(smem_b + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // A: K-major SW128, rows 128 B apart, 8-row groups 1024 B apart; +32 B per K=16 step.
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            // B: MN-major SW128, 64-column chunks 8 KB apart (LBO), 8-row K groups 1024 B apart
+            // (SBO); +16 rows * 128 B per K=16 step.
+            const uint64_t bdesc = smem_desc_sw128(b_addr + k * 2048, B_CHUNK_BYTES, 1024);
+            umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            issued = true;
+          }
+          umma_commit(&st->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&st->tmem_full[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        // Abort path: wait (bounded) for every MMA already issued before TMEM is released.
+        umma_commit(&st->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = (N % 8) == 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      if (!mbar_wait_bounded(&st->tmem_full[acc], acc_phase, abort_flag, err_word, kErrGemmEpilogueWait)) break;
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      __nv_bfloat16* crow = C + static_cast<long long>(row) * N;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c0, r);
+        tmem_wait_ld();
+        const int col = nb * BN + c0;
+        if (row < M && col < N) {
+          if (vec_ok && col + 32 <= N) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1]));
+              v.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3]));
+              v.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5]));
+              v.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7]));
+              dst[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col + j < N) crow[col + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->tmem_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---- host side ------------------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+// Resolves cuTensorMapEncodeTiled through the runtime so the library needs no -lcuda.
+void* tensor_map_encoder() {
+  static void* fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = p;
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with leading dimension ld (elements),
+// box [box_rows, box_cols], 128-byte swizzle, zero fill out of bounds.
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                       uint32_t box_rows, uint32_t box_cols) {
+  auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool gemm_bf16_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return m > 0 && k > 0 && n > 0 && (k % 8) == 0 && (n % 8) == 0 && al(a) && al(b) && al(c) &&
+         tensor_map_encoder() != nullptr;
+}
+
+cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                         cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  CUtensorMap ma, mb;
+  if (!make_tmap_bf16_2d(&ma, a, m, k, k, BM, BK)) return cudaErrorInvalidValue;
+  if (!make_tmap_bf16_2d(&mb, b, k, n, n, BK, 64)) return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent attribute set
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, c, m, n, k, ctx->err_word);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                      cudaStream_t s) {
+  if (gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_tc(a, b, c, m, k, n, s);
+  return gemm_bf16_simt(a, b, c, m, k, n, s);
+}
+
+}  // namespace lcb

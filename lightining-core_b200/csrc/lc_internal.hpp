@@ -1,0 +1,65 @@
+// Host-side internal interface between the C ABI (lc_api.cpp) and the kernel launchers.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace lcb {
+
+// Per-device state, created lazily on first use with that device current.
+struct DeviceCtx {
+  int device = -1;
+  int sm_count = 0;
+  unsigned* err_word = nullptr;  // device word written by kernels whose bounded waits gave up
+};
+DeviceCtx* device_ctx();
+
+// ---- GEMM ---------------------------------------------------------------------------------
+// Strict fp32 SIMT GEMM, C[m,n] = A[m,k] B[k,n], row-major.
+cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s);
+// bf16 in, fp32 accumulate, bf16 out.  tcgen05/TMA kernel when k%8==0 && n%8==0 and the
+// pointers are 16-byte aligned; otherwise a SIMT kernel with the same arithmetic contract.
+cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                      cudaStream_t s);
+cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                           cudaStream_t s);
+bool gemm_bf16_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n);
+cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                         cudaStream_t s);
+
+// ---- conv ---------------------------------------------------------------------------------
+// Implicit-GEMM NCHW conv, fp32 strict; bias may be null.  Output NCHW, so channel blocks of an
+// image are the raw [seq, d] slices the integrated pipeline reads as Q/K/V (no layout pass).
+cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
+                            int relu, cudaStream_t s);
+// Cyclic repeat of the first `have` floats of src into dst[0, total) (qkv_pack short case).
+cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s);
+
+// ---- attention ------------------------------------------------------------------------------
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  long long q_unit_stride, k_unit_stride, v_unit_stride, out_unit_stride;  // elements
+  int units, seq, d, causal;
+  float scale;           // softmax scale (1/sqrt(d))
+  float post_scale, post_bias;
+  int post_relu;         // out = relu?(out*post_scale + post_bias)
+  const float* proj_w;   // optional [d, proj_cols] fused projection (fp32 path only)
+  int proj_cols;
+};
+cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s);
+cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s);
+cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s);
+bool attention_bf16_tc_supported(const AttnArgs& a);
+
+// ---- elementwise ----------------------------------------------------------------------------
+cudaError_t vector_add_f32(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
+cudaError_t vector_add_f64(const double* a, const double* b, double* out, size_t n, cudaStream_t s);
+cudaError_t layer_norm_f32(const float* x, float* out, size_t rows, size_t cols, float eps, cudaStream_t s);
+
+}  // namespace lcb

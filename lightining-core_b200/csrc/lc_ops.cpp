@@ -1,0 +1,361 @@
+// Op half of the C ABI: attention / matmul2d / conv2d / integrated conv->attention / vector add /
+// layer norm entry points with the reference's IO-policy semantics mapped onto explicit device
+// memory (see include/lc_b200.h for the pointer conventions).  No CPU compute path exists here:
+// every op runs on the GPU or returns an error.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "lc_host.hpp"
+#include "lc_internal.hpp"
+
+namespace lcb {
+namespace {
+
+// Per-thread, per-device staging buffers for host-pointer (upload/download) calls; they grow
+// by 1.5x like the reference's Metal buffers (src/attention_metal.mm:1082) and are reused.
+struct Staging {
+  struct Slot {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+  };
+  std::vector<Slot> slots[64];
+  ~Staging() {
+    // Buffers are released with the thread; contexts may already be gone at process exit.
+  }
+  cudaError_t get(int dev, int slot, size_t bytes, void** out) {
+    auto& v = slots[dev];
+    if (static_cast<int>(v.size()) <= slot) v.resize(slot + 1);
+    Slot& s = v[slot];
+    if (s.bytes < bytes) {
+      if (s.ptr) cudaFree(s.ptr);
+      s.ptr = nullptr;
+      s.bytes = 0;
+      const size_t want = bytes + bytes / 2;
+      cudaError_t e = cudaMalloc(&s.ptr, want);
+      if (e != cudaSuccess) return e;
+      s.bytes = want;
+    }
+    *out = s.ptr;
+    return cudaSuccess;
+  }
+};
+thread_local Staging t_staging;
+
+// One call's host<->device plumbing.
+class Io {
+ public:
+  explicit Io(cudaStream_t s) : s_(s) { cudaGetDevice(&dev_); }
+  // Input: host pointer -> copied into staging slot; device pointer -> used directly.
+  cudaError_t in(const void* p, size_t bytes, bool host, const void** dev) {
+    if (!host) {
+      *dev = p;
+      return cudaSuccess;
+    }
+    void* d = nullptr;
+    cudaError_t e = t_staging.get(dev_, slot_++, bytes, &d);
+    if (e != cudaSuccess) return e;
+    e = cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, s_);
+    *dev = d;
+    return e;
+  }
+  // Output: host pointer -> a staging slot receives the result; device pointer -> direct.
+  cudaError_t out(void* p, size_t bytes, bool host, void** dev) {
+    if (!host) {
+      *dev = p;
+      return cudaSuccess;
+    }
+    return t_staging.get(dev_, slot_++, bytes, dev);
+  }
+  cudaError_t scratch(size_t bytes, void** dev) { return t_staging.get(dev_, slot_++, bytes, dev); }
+  cudaError_t finish(void* host_out, const void* dev_out, size_t bytes, bool download, bool sync) {
+    cudaError_t e = cudaSuccess;
+    if (download) e = cudaMemcpyAsync(host_out, dev_out, bytes, cudaMemcpyDeviceToHost, s_);
+    if (e != cudaSuccess) return e;
+    if (sync || download) e = cudaStreamSynchronize(s_);
+    return e;
+  }
+  cudaStream_t stream() const { return s_; }
+
+ private:
+  cudaStream_t s_;
+  int dev_ = 0;
+  int slot_ = 0;
+};
+
+// After a synchronizing call, a kernel that gave up a bounded wait shows in the error word.
+lcError_t check_error_word(bool synced) {
+  if (!synced) return LC_SUCCESS;
+  DeviceCtx* c = device_ctx();
+  if (!c) return LC_NOT_INITIALIZED;
+  unsigned w = 0;
+  if (cudaMemcpy(&w, c->err_word, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess) return LC_DRIVER_ERROR;
+  return w ? LC_DRIVER_ERROR : LC_SUCCESS;
+}
+
+#define LC_TRY(expr)                                   \
+  do {                                                 \
+    cudaError_t e_ = (expr);                           \
+    if (e_ != cudaSuccess) return from_cuda(e_);       \
+  } while (0)
+
+size_t elem_size(lcDataType t) { return t == LC_DTYPE_BF16 ? 2 : t == LC_DTYPE_F64 ? 8 : 4; }
+
+}  // namespace
+}  // namespace lcb
+
+using namespace lcb;
+
+extern "C" {
+
+void lcAttentionIoPolicyDefault(lcAttentionIoPolicy* p) {
+  if (!p) return;
+  p->upload_q = p->upload_k = p->upload_v = p->upload_target = 1;
+  p->download_out = p->download_v = p->synchronize = 1;
+  p->loss_every = 1;
+  p->output_scale = 1.0f;
+  p->output_bias = 0.0f;
+  p->output_relu = 0;
+}
+void lcMatMulIoPolicyDefault(lcMatMulIoPolicy* p) {
+  if (p) p->upload_a = p->upload_b = p->download_out = p->synchronize = 1;
+}
+void lcConv2dIoPolicyDefault(lcConv2dIoPolicy* p) {
+  if (p) p->upload_x = p->upload_w = p->upload_bias = p->download_out = p->synchronize = 1;
+}
+void lcVectorAddIoPolicyDefault(lcVectorAddIoPolicy* p) {
+  if (p) p->upload_a = p->upload_b = p->download_out = p->synchronize = 1;
+}
+
+void lcMatMulPolicyForStage(lcLoopStage stage, lcMatMulIoPolicy* p) {
+  if (!p) return;
+  const int start = stage == LC_LOOP_START;
+  p->upload_a = start;
+  p->upload_b = start;
+  p->download_out = stage == LC_LOOP_FINISH;
+  p->synchronize = stage == LC_LOOP_FINISH || stage == LC_LOOP_SYNC;
+}
+
+lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* out, size_t units, size_t seq,
+                             size_t head_dim, int causal, lcDataType dtype, const lcAttentionIoPolicy* policy,
+                             lcStream_t stream) {
+  if (!q || !k || !v || !out || units == 0 || seq == 0 || head_dim == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_BF16) return LC_NOT_SUPPORTED;
+  if (seq > (size_t)INT_MAX || head_dim > 256 || units > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  lcAttentionIoPolicy pol;
+  if (policy) {
+    pol = *policy;
+  } else {
+    lcAttentionIoPolicyDefault(&pol);
+    pol.upload_q = pol.upload_k = pol.upload_v = pol.download_out = pol.synchronize = 0;
+  }
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t es = elem_size(dtype);
+  const size_t bytes = units * seq * head_dim * es;
+  const void *dq, *dk, *dv;
+  void* dout;
+  LC_TRY(io.in(q, bytes, pol.upload_q, &dq));
+  LC_TRY(io.in(k, bytes, pol.upload_k, &dk));
+  LC_TRY(io.in(v, bytes, pol.upload_v, &dv));
+  LC_TRY(io.out(out, bytes, pol.download_out, &dout));
+  trace_op(kOpAttention, units * seq * seq * head_dim);
+
+  const long long ustride = static_cast<long long>(seq * head_dim);
+  for (size_t u0 = 0; u0 < units; u0 += 65535) {
+    const size_t n = units - u0 < 65535 ? units - u0 : 65535;
+    AttnArgs a{};
+    a.q = static_cast<const char*>(dq) + u0 * ustride * es;
+    a.k = static_cast<const char*>(dk) + u0 * ustride * es;
+    a.v = static_cast<const char*>(dv) + u0 * ustride * es;
+    a.out = static_cast<char*>(dout) + u0 * ustride * es;
+    a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = a.out_unit_stride = ustride;
+    a.units = static_cast<int>(n);
+    a.seq = static_cast<int>(seq);
+    a.d = static_cast<int>(head_dim);
+    a.causal = causal ? 1 : 0;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.post_scale = pol.output_scale;
+    a.post_bias = pol.output_bias;
+    a.post_relu = pol.output_relu ? 1 : 0;
+    LC_TRY(dtype == LC_DTYPE_F32 ? attention_f32(a, io.stream()) : attention_bf16(a, io.stream()));
+  }
+  LC_TRY(io.finish(out, dout, bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+lcError_t lcMatMul(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
+                   const lcMatMulIoPolicy* policy, lcStream_t stream) {
+  if (!a || !b || !out || m == 0 || k == 0 || n == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_BF16) return LC_NOT_SUPPORTED;
+  if (m > (size_t)INT_MAX || k > (size_t)INT_MAX || n > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  lcMatMulIoPolicy pol = {0, 0, 0, 0};
+  if (policy) pol = *policy;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t es = elem_size(dtype);
+  const void *da, *db;
+  void* dc;
+  LC_TRY(io.in(a, m * k * es, pol.upload_a, &da));
+  LC_TRY(io.in(b, k * n * es, pol.upload_b, &db));
+  LC_TRY(io.out(out, m * n * es, pol.download_out, &dc));
+  trace_op(kOpMatMul, m * k * n);
+  if (dtype == LC_DTYPE_F32) {
+    LC_TRY(gemm_f32(static_cast<const float*>(da), static_cast<const float*>(db), static_cast<float*>(dc), (int)m,
+                    (int)k, (int)n, io.stream()));
+  } else {
+    LC_TRY(gemm_bf16(static_cast<const __nv_bfloat16*>(da), static_cast<const __nv_bfloat16*>(db),
+                     static_cast<__nv_bfloat16*>(dc), (int)m, (int)k, (int)n, io.stream()));
+  }
+  LC_TRY(io.finish(out, dc, m * n * es, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+// Validation of include/lightning_core/core/ops.hpp:874-884.
+static bool conv_shape_ok(const void* x, const void* w, const void* out, size_t batch, size_t in_c, size_t in_h,
+                          size_t in_w, size_t out_c, size_t kh, size_t kw, size_t sh, size_t sw, size_t ph,
+                          size_t pw) {
+  if (!x || !w || !out || batch == 0 || in_c == 0 || in_h == 0 || in_w == 0 || out_c == 0 || kh == 0 || kw == 0 ||
+      sh == 0 || sw == 0)
+    return false;
+  return in_h + 2 * ph >= kh && in_w + 2 * pw >= kw;
+}
+
+lcError_t lcConv2dNchw(const float* x, const float* w, const float* bias, float* out, size_t batch,
+                       size_t in_channels, size_t in_h, size_t in_w, size_t out_channels, size_t kernel_h,
+                       size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w, int apply_relu,
+                       const lcConv2dIoPolicy* policy, lcStream_t stream) {
+  if (!conv_shape_ok(x, w, out, batch, in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w,
+                     pad_h, pad_w))
+    return LC_INVALID_VALUE;
+  const size_t oh = (in_h + 2 * pad_h - kernel_h) / stride_h + 1;
+  const size_t ow = (in_w + 2 * pad_w - kernel_w) / stride_w + 1;
+  if (batch * oh * ow > (size_t)INT_MAX || in_channels * kernel_h * kernel_w > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  lcConv2dIoPolicy pol = {0, 0, 0, 0, 0};
+  if (policy) pol = *policy;
+  Io io(static_cast<cudaStream_t>(stream));
+  const void *dx, *dw, *db = nullptr;
+  void* dout;
+  const size_t out_bytes = batch * out_channels * oh * ow * 4;
+  LC_TRY(io.in(x, batch * in_channels * in_h * in_w * 4, pol.upload_x, &dx));
+  LC_TRY(io.in(w, out_channels * in_channels * kernel_h * kernel_w * 4, pol.upload_w, &dw));
+  if (bias) LC_TRY(io.in(bias, out_channels * 4, pol.upload_bias, &db));
+  LC_TRY(io.out(out, out_bytes, pol.download_out, &dout));
+  trace_op(kOpConv2dNchw, batch * oh * ow * out_channels * in_channels * kernel_h * kernel_w);
+  LC_TRY(conv2d_nchw_f32(static_cast<const float*>(dx), static_cast<const float*>(dw),
+                         static_cast<const float*>(db), static_cast<float*>(dout), (int)batch, (int)in_channels,
+                         (int)in_h, (int)in_w, (int)out_channels, (int)kernel_h, (int)kernel_w, (int)stride_h,
+                         (int)stride_w, (int)pad_h, (int)pad_w, apply_relu ? 1 : 0, io.stream()));
+  LC_TRY(io.finish(out, dout, out_bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+lcError_t lcConvAttentionNchw(const float* x, const float* w, const float* bias, const float* proj_w, float* out,
+                              size_t batch, size_t in_channels, size_t in_h, size_t in_w, size_t out_channels,
+                              size_t kernel_h, size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h,
+                              size_t pad_w, size_t seq, size_t head_dim, size_t proj_cols, int per_image,
+                              const lcConv2dIoPolicy* policy, lcStream_t stream) {
+  if (!conv_shape_ok(x, w, out, batch, in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w,
+                     pad_h, pad_w) ||
+      seq == 0 || head_dim == 0 || (proj_w && proj_cols == 0))
+    return LC_INVALID_VALUE;
+  if (head_dim > 256 || (proj_w && (head_dim > 128 || proj_cols > 128)) || seq > (size_t)INT_MAX)
+    return LC_NOT_SUPPORTED;
+  const size_t oh = (in_h + 2 * pad_h - kernel_h) / stride_h + 1;
+  const size_t ow = (in_w + 2 * pad_w - kernel_w) / stride_w + 1;
+  if (batch * oh * ow > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  lcConv2dIoPolicy pol = {0, 0, 0, 0, 0};
+  if (policy) pol = *policy;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t img = out_channels * oh * ow;  // conv floats per image
+  const size_t need = seq * head_dim;
+  const size_t cols = proj_w ? proj_cols : head_dim;
+  const size_t units = per_image ? batch : 1;
+  const size_t out_bytes = units * seq * cols * 4;
+  const void *dx, *dw, *db = nullptr, *dp = nullptr;
+  void *dout, *conv;
+  LC_TRY(io.in(x, batch * in_channels * in_h * in_w * 4, pol.upload_x, &dx));
+  LC_TRY(io.in(w, out_channels * in_channels * kernel_h * kernel_w * 4, pol.upload_w, &dw));
+  if (bias) LC_TRY(io.in(bias, out_channels * 4, pol.upload_bias, &db));
+  if (proj_w) LC_TRY(io.in(proj_w, head_dim * proj_cols * 4, pol.upload_w, &dp));
+  LC_TRY(io.out(out, out_bytes, pol.download_out, &dout));
+  LC_TRY(io.scratch(batch * img * 4, &conv));
+  cudaStream_t s = io.stream();
+  trace_op(kOpConv2dNchw, batch * oh * ow * out_channels * in_channels * kernel_h * kernel_w);
+  // Conv + bias + ReLU; its NCHW output already is the QKV arrangement (raw channel-block slices).
+  LC_TRY(conv2d_nchw_f32(static_cast<const float*>(dx), static_cast<const float*>(dw), static_cast<const float*>(db),
+                         static_cast<float*>(conv), (int)batch, (int)in_channels, (int)in_h, (int)in_w,
+                         (int)out_channels, (int)kernel_h, (int)kernel_w, (int)stride_h, (int)stride_w, (int)pad_h,
+                         (int)pad_w, 1, s));
+  const float* qkv = static_cast<const float*>(conv);
+  long long unit_stride = static_cast<long long>(img);
+  const size_t avail = per_image ? img : batch * img;
+  if (avail < 3 * need) {
+    // Short conv output: the reference repeats the flat buffer cyclically up to 3*need floats
+    // (python/bindings/bind_integrated.cpp:718-728).  Only this rare case pays a packing pass.
+    void* packed;
+    LC_TRY(io.scratch(units * 3 * need * 4, &packed));
+    for (size_t u = 0; u < units; ++u)
+      LC_TRY(repeat_fill_f32(qkv + u * img, avail, static_cast<float*>(packed) + u * 3 * need, 3 * need, s));
+    qkv = static_cast<const float*>(packed);
+    unit_stride = static_cast<long long>(3 * need);
+  }
+  trace_op(kOpAttention, units * seq * seq * head_dim);
+  for (size_t u0 = 0; u0 < units; u0 += 65535) {
+    const size_t n = units - u0 < 65535 ? units - u0 : 65535;
+    AttnArgs a{};
+    a.q = qkv + u0 * unit_stride;
+    a.k = qkv + u0 * unit_stride + need;
+    a.v = qkv + u0 * unit_stride + 2 * need;
+    a.out = static_cast<float*>(dout) + u0 * seq * cols;
+    a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = unit_stride;
+    a.out_unit_stride = static_cast<long long>(seq * cols);
+    a.units = static_cast<int>(n);
+    a.seq = static_cast<int>(seq);
+    a.d = static_cast<int>(head_dim);
+    a.causal = 0;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.post_scale = 1.0f;
+    a.post_bias = 0.0f;
+    a.post_relu = 0;
+    a.proj_w = static_cast<const float*>(dp);
+    a.proj_cols = static_cast<int>(proj_cols);
+    LC_TRY(attention_f32(a, s));
+  }
+  LC_TRY(io.finish(out, dout, out_bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataType dtype,
+                      const lcVectorAddIoPolicy* policy, lcStream_t stream) {
+  if (!a || !b || !out || n == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_F64) return LC_NOT_SUPPORTED;
+  lcVectorAddIoPolicy pol = {0, 0, 0, 0};
+  if (policy) pol = *policy;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t bytes = n * elem_size(dtype);
+  const void *da, *db;
+  void* dc;
+  LC_TRY(io.in(a, bytes, pol.upload_a, &da));
+  LC_TRY(io.in(b, bytes, pol.upload_b, &db));
+  LC_TRY(io.out(out, bytes, pol.download_out, &dc));
+  trace_op(kOpVectorAdd, n);
+  if (dtype == LC_DTYPE_F32)
+    LC_TRY(vector_add_f32(static_cast<const float*>(da), static_cast<const float*>(db), static_cast<float*>(dc), n,
+                          io.stream()));
+  else
+    LC_TRY(vector_add_f64(static_cast<const double*>(da), static_cast<const double*>(db), static_cast<double*>(dc), n,
+                          io.stream()));
+  LC_TRY(io.finish(out, dc, bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, float eps, lcStream_t stream) {
+  if (!x || !out || rows == 0 || cols == 0) return LC_INVALID_VALUE;
+  LC_TRY(layer_norm_f32(x, out, rows, cols, eps, static_cast<cudaStream_t>(stream)));
+  return LC_SUCCESS;
+}
+
+}  // extern "C"

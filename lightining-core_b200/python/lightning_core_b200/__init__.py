@@ -1,0 +1,383 @@
+"""Python face of liblc_b200.so -- the B200 build of Lightning Core's attention / matmul2d /
+conv->attention hot path.
+
+Mirrors the reference's pybind surface for that path (python/bindings/bind_attention.cpp:298-366,
+bind_ops.cpp:728-760 and 1164-1210, bind_integrated.cpp:958-1140): same function names, argument
+meaning and errors (ValueError for bad shapes, RuntimeError carrying lcGetErrorString for a
+failed status).  The only device is "cuda"; there is no CPU compute path, so "cpu"/"metal"
+raise ValueError.  The library must be built (``make -C lightining-core_b200``); importing this
+module without it raises ImportError -- nothing falls back to NumPy.
+
+bf16 tensors are passed as ``numpy.uint16`` arrays holding the bf16 bit patterns
+(see :func:`to_bf16` / :func:`from_bf16`).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_PKG_ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), "..", ".."))
+LIB_PATH = os.path.join(_PKG_ROOT, "liblc_b200.so")
+
+if not os.path.exists(LIB_PATH):
+    raise ImportError(f"{LIB_PATH} is not built; run `make -C {_PKG_ROOT}`")
+
+lib = C.CDLL(LIB_PATH)
+
+# ---- enums (include/lc_b200.h) ---------------------------------------------------------------
+LC_SUCCESS, LC_NOT_INITIALIZED, LC_INVALID_VALUE, LC_OUT_OF_MEMORY, LC_NOT_SUPPORTED, LC_DRIVER_ERROR, LC_UNKNOWN = range(7)
+H2H, H2D, D2H, D2D = range(4)
+F32, BF16, F64 = 0, 1, 2
+LOOP_START, LOOP_RUN, LOOP_FINISH, LOOP_SYNC = range(4)
+
+
+class AttentionIoPolicy(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("upload_q", "upload_k", "upload_v", "upload_target", "download_out",
+                                       "download_v", "synchronize", "loss_every")] + [
+        ("output_scale", C.c_float), ("output_bias", C.c_float), ("output_relu", C.c_int)]
+
+
+class MatMulIoPolicy(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("upload_a", "upload_b", "download_out", "synchronize")]
+
+
+class VectorAddIoPolicy(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("upload_a", "upload_b", "download_out", "synchronize")]
+
+
+class Conv2dIoPolicy(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("upload_x", "upload_w", "upload_bias", "download_out", "synchronize")]
+
+
+class RuntimeTraceEvent(C.Structure):
+    _fields_ = [("type", C.c_int), ("status", C.c_int), ("timestamp_ns", C.c_uint64), ("size_bytes", C.c_size_t),
+                ("detail0", C.c_int), ("detail1", C.c_int)]
+
+
+_vp, _sz, _i, _f = C.c_void_p, C.c_size_t, C.c_int, C.c_float
+_SIGS = {
+    "lcMalloc": (_i, [C.POINTER(_vp), _sz]),
+    "lcFree": (_i, [_vp]),
+    "lcMemcpy": (_i, [_vp, _vp, _sz, _i]),
+    "lcDeviceSynchronize": (_i, []),
+    "lcGetDeviceCount": (_i, [C.POINTER(_i)]),
+    "lcIsCudaAvailable": (_i, []),
+    "lcIsMetalAvailable": (_i, []),
+    "lcGetApiVersionString": (C.c_char_p, []),
+    "lcGetApiVersion": (_i, [C.POINTER(_i)] * 3),
+    "lcGetErrorString": (C.c_char_p, [_i]),
+    "lcBackendName": (C.c_char_p, []),
+    "lcGetStructSize": (_sz, [_i]),
+    "lcCheckStructSize": (_i, [_i, _sz]),
+    "lcGetMemoryModel": (_i, []),
+    "lcGetMemoryModelName": (C.c_char_p, [_i]),
+    "lcAttentionIoPolicyDefault": (None, [C.POINTER(AttentionIoPolicy)]),
+    "lcMatMulIoPolicyDefault": (None, [C.POINTER(MatMulIoPolicy)]),
+    "lcConv2dIoPolicyDefault": (None, [C.POINTER(Conv2dIoPolicy)]),
+    "lcVectorAddIoPolicyDefault": (None, [C.POINTER(VectorAddIoPolicy)]),
+    "lcMatMulPolicyForStage": (None, [_i, C.POINTER(MatMulIoPolicy)]),
+    "lcAttentionForward": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcMatMul": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, C.POINTER(MatMulIoPolicy), _vp]),
+    "lcConv2dNchw": (_i, [_vp, _vp, _vp, _vp] + [_sz] * 11 + [_i, C.POINTER(Conv2dIoPolicy), _vp]),
+    "lcConvAttentionNchw": (_i, [_vp] * 5 + [_sz] * 14 + [_i, C.POINTER(Conv2dIoPolicy), _vp]),
+    "lcVectorAdd": (_i, [_vp, _vp, _vp, _sz, _i, C.POINTER(VectorAddIoPolicy), _vp]),
+    "lcLayerNorm": (_i, [_vp, _vp, _sz, _sz, _f, _vp]),
+    "lcGetDeviceErrorWord": (_i, [C.POINTER(C.c_uint)]),
+    "lcClearDeviceErrorWord": (_i, []),
+    "lcRuntimeTraceSetEnabled": (None, [_i]),
+    "lcRuntimeTraceIsEnabled": (_i, []),
+    "lcRuntimeTraceClear": (None, []),
+    "lcRuntimeTraceCount": (_sz, []),
+    "lcRuntimeTraceCapacity": (_sz, []),
+    "lcRuntimeTraceGet": (_i, [_sz, C.POINTER(RuntimeTraceEvent)]),
+}
+for _name, (_res, _args) in _SIGS.items():
+    _fn = getattr(lib, _name)
+    _fn.restype = _res
+    _fn.argtypes = _args
+
+
+class LightningError(RuntimeError):
+    def __init__(self, code: int, what: str = ""):
+        self.code = code
+        msg = lib.lcGetErrorString(code).decode()
+        super().__init__(f"{what}: {msg}" if what else msg)
+
+
+def check(code: int, what: str = "") -> None:
+    if code != LC_SUCCESS:
+        raise LightningError(code, what)
+
+
+def cuda_available() -> bool:
+    return bool(lib.lcIsCudaAvailable())
+
+
+def api_version() -> str:
+    return lib.lcGetApiVersionString().decode()
+
+
+# ---- bf16 helpers ---------------------------------------------------------------------------
+def to_bf16(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns (uint16), round to nearest even."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    nan = (u & 0x7F800000) == 0x7F800000
+    nan &= (u & 0x007FFFFF) != 0
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def from_bf16(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+# ---- device memory --------------------------------------------------------------------------
+class DeviceBuffer:
+    """A cudaMalloc'd buffer owned from Python (lcMalloc / lcFree)."""
+
+    def __init__(self, nbytes: int):
+        self.nbytes = int(nbytes)
+        self.ptr = C.c_void_p()
+        check(lib.lcMalloc(C.byref(self.ptr), max(1, self.nbytes)), "lcMalloc")
+
+    @classmethod
+    def from_array(cls, a: np.ndarray) -> "DeviceBuffer":
+        a = np.ascontiguousarray(a)
+        buf = cls(a.nbytes)
+        buf.upload(a)
+        return buf
+
+    @property
+    def value(self) -> int:
+        return self.ptr.value
+
+    def upload(self, a: np.ndarray) -> None:
+        a = np.ascontiguousarray(a)
+        assert a.nbytes <= self.nbytes
+        check(lib.lcMemcpy(self.ptr, a.ctypes.data_as(C.c_void_p), a.nbytes, H2D), "lcMemcpy H2D")
+
+    def download(self, shape, dtype) -> np.ndarray:
+        out = np.empty(shape, dtype=dtype)
+        check(lib.lcMemcpy(out.ctypes.data_as(C.c_void_p), self.ptr, out.nbytes, D2H), "lcMemcpy D2H")
+        return out
+
+    def free(self) -> None:
+        if self.ptr is not None and self.ptr.value:
+            lib.lcFree(self.ptr)
+        self.ptr = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---- reference-mirroring ops ------------------------------------------------------------------
+def _parse_device(device: str) -> None:
+    if device not in ("cuda", "gpu"):
+        raise ValueError(f"device '{device}' is not served by the B200 build (only 'cuda'; no CPU path)")
+
+
+def _f32(a, name):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a
+
+
+def _vp(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def _require_2d(a, name):
+    if a.ndim != 2:
+        raise ValueError(f"{name} must be a 2D float32 array shaped [seq_len, head_dim]")
+    return a.shape
+
+
+def attention2d_into(q, k, v, out, causal: bool = False, device: str = "cuda", policy: AttentionIoPolicy = None):
+    """bind_attention.cpp:329-366: out[seq, d] = softmax(q k^T / sqrt(d)) v (host arrays)."""
+    _parse_device(device)
+    q, k, v = _f32(q, "q"), _f32(k, "k"), _f32(v, "v")
+    s, d = _require_2d(q, "q")
+    if _require_2d(k, "k") != (s, d) or _require_2d(v, "v") != (s, d):
+        raise ValueError("q/k/v must have identical 2D shape [seq_len, head_dim]")
+    if out.dtype != np.float32 or out.shape != (s, d) or not out.flags["C_CONTIGUOUS"]:
+        raise ValueError("out must be a 2D float32 array shaped [seq_len, head_dim]")
+    pol = policy or default_attention_policy()
+    check(lib.lcAttentionForward(_vp(q), _vp(k), _vp(v), _vp(out), 1, s, d, int(causal), F32, C.byref(pol), None),
+          "attention2d")
+    return out
+
+
+def attention2d(q, k, v, causal: bool = False, device: str = "cuda", policy: AttentionIoPolicy = None):
+    """bind_attention.cpp:298-327."""
+    q = _f32(q, "q")
+    if q.ndim != 2:
+        raise ValueError("q must be a 2D float32 array shaped [seq_len, head_dim]")
+    out = np.empty(q.shape, np.float32)
+    return attention2d_into(q, k, v, out, causal, device, policy)
+
+
+def attention_batched(q, k, v, causal: bool = False, dtype: int = F32):
+    """Host [units, seq, d] arrays (float32, or uint16 bf16 bits with dtype=BF16)."""
+    q = np.ascontiguousarray(q)
+    units, s, d = q.shape
+    out = np.empty_like(q)
+    pol = default_attention_policy()
+    check(lib.lcAttentionForward(_vp(q), _vp(np.ascontiguousarray(k)), _vp(np.ascontiguousarray(v)), _vp(out),
+                                 units, s, d, int(causal), dtype, C.byref(pol), None), "attention")
+    return out
+
+
+def default_attention_policy() -> AttentionIoPolicy:
+    p = AttentionIoPolicy()
+    lib.lcAttentionIoPolicyDefault(C.byref(p))
+    return p
+
+
+def default_matmul_policy() -> MatMulIoPolicy:
+    p = MatMulIoPolicy()
+    lib.lcMatMulIoPolicyDefault(C.byref(p))
+    return p
+
+
+def matmul_policy_for_stage(stage: int) -> MatMulIoPolicy:
+    p = MatMulIoPolicy()
+    lib.lcMatMulPolicyForStage(stage, C.byref(p))
+    return p
+
+
+def matmul2d_into(a, b, out, device: str = "cuda", dtype: int = F32):
+    """bind_ops.cpp:1187-1210."""
+    _parse_device(device)
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    if a.ndim != 2 or b.ndim != 2:
+        raise ValueError("matmul2d expects 2D arrays")
+    m, kk = a.shape
+    if b.shape[0] != kk:
+        raise ValueError("matmul2d_into shape mismatch: a.shape[1] must equal b.shape[0]")
+    n = b.shape[1]
+    if out.size != m * n or not out.flags["C_CONTIGUOUS"]:
+        raise ValueError("out must be [m, n] or flat m*n")
+    pol = default_matmul_policy()
+    check(lib.lcMatMul(_vp(a), _vp(b), _vp(out), m, kk, n, dtype, C.byref(pol), None), "matmul2d")
+    return out
+
+
+def matmul2d(a, b, device: str = "cuda", dtype: int = F32):
+    """bind_ops.cpp:1164-1185 (float32), or bf16 bits (uint16) with dtype=BF16."""
+    if dtype == F32:
+        a = _f32(a, "a")
+        b = _f32(b, "b")
+    if np.ndim(a) != 2 or np.ndim(b) != 2:
+        raise ValueError("matmul2d expects 2D arrays")
+    if a.shape[1] != b.shape[0]:
+        raise ValueError("matmul2d shape mismatch: a.shape[1] must equal b.shape[0]")
+    out = np.empty((a.shape[0], b.shape[1]), np.float32 if dtype == F32 else np.uint16)
+    return matmul2d_into(a, b, out, device, dtype)
+
+
+def _conv_dims(x, w, stride_h, stride_w, pad_h, pad_w):
+    if x.ndim != 4 or w.ndim != 4:
+        raise ValueError("x and w must be 4D arrays (NCHW and OIHW)")
+    n, c, h, wd = x.shape
+    oc, wc, kh, kw = w.shape
+    if c != wc:
+        raise ValueError("x channels and w in_channels mismatch")
+    if stride_h == 0 or stride_w == 0:
+        raise ValueError("stride must be > 0")
+    if h + 2 * pad_h < kh or wd + 2 * pad_w < kw:
+        raise ValueError("invalid padding/kernel for input size")
+    return n, c, h, wd, oc, kh, kw, (h + 2 * pad_h - kh) // stride_h + 1, (wd + 2 * pad_w - kw) // stride_w + 1
+
+
+def conv2d_nchw(x, w, bias=None, stride_h=1, stride_w=1, pad_h=0, pad_w=0, device="cuda", apply_relu=False):
+    """bind_ops.cpp:728-800 (+ the apply_relu flag of ops::conv2dNchw)."""
+    _parse_device(device)
+    x, w = _f32(x, "x"), _f32(w, "w")
+    n, c, h, wd, oc, kh, kw, oh, ow = _conv_dims(x, w, stride_h, stride_w, pad_h, pad_w)
+    if bias is not None:
+        bias = _f32(bias, "bias")
+        if bias.size != oc:
+            raise ValueError("bias shape mismatch")
+    out = np.empty((n, oc, oh, ow), np.float32)
+    pol = Conv2dIoPolicy()
+    lib.lcConv2dIoPolicyDefault(C.byref(pol))
+    check(lib.lcConv2dNchw(_vp(x), _vp(w), _vp(bias), _vp(out), n, c, h, wd, oc, kh, kw, stride_h, stride_w, pad_h,
+                           pad_w, int(apply_relu), C.byref(pol), None), "conv2d_nchw")
+    return out
+
+
+def lightning_conv_attention_torchstrong_nchw_into(x, w, bias, out, seq_len, head_dim, stride_h=1, stride_w=1,
+                                                   pad_h=0, pad_w=0, device="cuda", execution_mode="eager",
+                                                   proj_w=None, per_image=False):
+    """bind_integrated.cpp:614-730 (+ optional projection, graph.hpp:3529-3547).
+
+    per_image=False keeps the reference's batch semantics (one attention over the first
+    3*seq*d floats of the flat conv output); per_image=True runs them on each image."""
+    _parse_device(device)
+    if execution_mode not in ("eager", "graph"):
+        raise ValueError("execution_mode must be 'eager' or 'graph'")
+    x, w = _f32(x, "x"), _f32(w, "w")
+    n, c, h, wd, oc, kh, kw, oh, ow = _conv_dims(x, w, stride_h, stride_w, pad_h, pad_w)
+    if bias is not None:
+        bias = _f32(bias, "bias")
+        if bias.size != oc:
+            raise ValueError("bias shape mismatch")
+    cols = head_dim
+    if proj_w is not None:
+        proj_w = _f32(proj_w, "proj_w")
+        if proj_w.ndim != 2 or proj_w.shape[0] != head_dim:
+            raise ValueError("proj_w must be [head_dim, out_cols]")
+        cols = proj_w.shape[1]
+    units = n if per_image else 1
+    if out.dtype != np.float32 or out.size != units * seq_len * cols or not out.flags["C_CONTIGUOUS"]:
+        raise ValueError("out size mismatch")
+    pol = Conv2dIoPolicy()
+    lib.lcConv2dIoPolicyDefault(C.byref(pol))
+    check(lib.lcConvAttentionNchw(_vp(x), _vp(w), _vp(bias), _vp(proj_w), _vp(out), n, c, h, wd, oc, kh, kw,
+                                  stride_h, stride_w, pad_h, pad_w, seq_len, head_dim, cols, int(per_image),
+                                  C.byref(pol), None), "conv_attention")
+    return out
+
+
+def lightning_conv_attention_torchstrong_nchw(x, w, bias, seq_len, head_dim, stride_h=1, stride_w=1, pad_h=0,
+                                              pad_w=0, device="cuda", execution_mode="eager", proj_w=None,
+                                              per_image=False):
+    """bind_integrated.cpp:958-1140: returns the flat [seq*cols] (or [batch, seq, cols]) result."""
+    cols = head_dim if proj_w is None else np.shape(proj_w)[1]
+    units = np.shape(x)[0] if per_image else 1
+    out = np.empty(units * seq_len * cols, np.float32)
+    lightning_conv_attention_torchstrong_nchw_into(x, w, bias, out, seq_len, head_dim, stride_h, stride_w, pad_h,
+                                                   pad_w, device, execution_mode, proj_w, per_image)
+    return out.reshape(units, seq_len, cols) if per_image else out
+
+
+def vector_add(a, b, device="cuda"):
+    """bind_ops.cpp:1098-1125 (float32 or float64)."""
+    _parse_device(device)
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    if a.shape != b.shape or a.dtype != b.dtype or a.dtype not in (np.float32, np.float64):
+        raise ValueError("vector_add expects two same-shape float32/float64 arrays")
+    out = np.empty_like(a)
+    pol = VectorAddIoPolicy()
+    lib.lcVectorAddIoPolicyDefault(C.byref(pol))
+    check(lib.lcVectorAdd(_vp(a), _vp(b), _vp(out), a.size, F32 if a.dtype == np.float32 else F64, C.byref(pol),
+                          None), "vector_add")
+    return out
+
+
+def layer_norm(x, eps=1e-5):
+    """The reference benchmark's LN (README.md:2267-2270) over the last axis, on the GPU."""
+    x = _f32(x, "x")
+    rows, cols = x.reshape(-1, x.shape[-1]).shape
+    dx = DeviceBuffer.from_array(x)
+    dy = DeviceBuffer(x.nbytes)
+    check(lib.lcLayerNorm(dx.ptr, dy.ptr, rows, cols, eps, None), "layer_norm")
+    check(lib.lcDeviceSynchronize(), "sync")
+    return dy.download(x.shape, np.float32)
