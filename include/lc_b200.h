@@ -226,6 +226,23 @@ lcError_t lcConvAttentionNchw(const float* x, const float* w, const float* bias,
                               size_t pad_w, size_t seq, size_t head_dim, size_t proj_cols, int per_image,
                               const lcConv2dIoPolicy* policy, lcStream_t stream);
 
+/* No counterpart in the reference.  lcConvAttentionNchw for callers that cannot allocate GPU
+ * memory (code running where cudaMalloc may not be called -- a host callback, a real-time loop,
+ * a plugin whose host owns every device allocation).  Same arguments and results as
+ * lcConvAttentionNchw, but every pointer is a DEVICE pointer (no IO policy) and the conv
+ * intermediate lives in a fixed 64 MiB array compiled into the library (16 Mi floats), which
+ * every GPU that loads the library holds until exit.  Needs batch*out_channels*out_h*out_w
+ * floats of it (plus units*3*seq*head_dim when the conv output is shorter than 3*seq*head_dim);
+ * larger calls return LC_INVALID_VALUE.  Allocates nothing: no cudaMalloc/cudaFree.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture.  All calls share the array: calls that overlap on the
+ * GPU race -- keep them on one stream.  Asynchronous on `stream`. */
+lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, const float* bias, const float* proj_w,
+                                     float* out, size_t batch, size_t in_channels, size_t in_h, size_t in_w,
+                                     size_t out_channels, size_t kernel_h, size_t kernel_w, size_t stride_h,
+                                     size_t stride_w, size_t pad_h, size_t pad_w, size_t seq, size_t head_dim,
+                                     size_t proj_cols, int per_image, lcStream_t stream);
+
 /* out = a + b (f32 or f64); replaces vectorAddCuda (src/ops/vector_add_cuda.cu:12-86). */
 lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataType dtype,
                       const lcVectorAddIoPolicy* policy, lcStream_t stream);

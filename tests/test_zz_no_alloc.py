@@ -1,0 +1,70 @@
+"""lcConvAttentionNchwNoAlloc -- the pipeline entry point for callers that cannot allocate GPU
+memory (the caller owns every device buffer; the library uses only its fixed scratch array).
+
+Checked through the C ABI against lcConvAttentionNchw on the same device buffers, twice in a row
+(the shared scratch keeps the previous call's contents, which must not leak into the next).
+Collected last on purpose: a failure here leaves every other test already run."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import close_enough
+
+pytestmark = pytest.mark.gpu
+F32_TOL = (1e-4, 1e-4)
+SCRATCH_FLOATS = 16 * 1024 * 1024
+
+
+def _bind(lc):
+    fn = lc.lib.lcConvAttentionNchwNoAlloc
+    fn.restype = C.c_int
+    fn.argtypes = [C.c_void_p] * 5 + [C.c_size_t] * 14 + [C.c_int, C.c_void_p]
+    return fn
+
+
+def _case(seed, n, c, h, w_, oc, seq, d, proj):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((n, c, h, w_)).astype(np.float32)
+    w = rng.uniform(-0.2, 0.2, (oc, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, oc).astype(np.float32)
+    pw = rng.uniform(-0.3, 0.3, (d, proj)).astype(np.float32) if proj else None
+    return x, w, bias, pw
+
+
+@pytest.mark.parametrize("per_image", [1, 0])
+def test_no_alloc_matches_allocating_entry_point(gpu, per_image):
+    fn = _bind(gpu)
+    L = gpu.lib
+    cases = [(1, 4, 64, 28, 28, 192, 784, 64, 64),  # raw channel-block QKV slices, projection 64x64
+             (2, 3, 8, 12, 12, 24, 144, 16, 0)]     # short conv output -> cyclic repeat, no projection
+    for seed, n, c, h, w_, oc, seq, d, proj in cases:
+        x, w, bias, pw = _case(seed, n, c, h, w_, oc, seq, d, proj)
+        cols = proj or d
+        units = n if per_image else 1
+        bufs = {k: gpu.DeviceBuffer.from_array(v) for k, v in (("x", x), ("w", w), ("b", bias)) }
+        dpw = gpu.DeviceBuffer.from_array(pw) if pw is not None else None
+        out_a = gpu.DeviceBuffer(units * seq * cols * 4)
+        out_b = gpu.DeviceBuffer(units * seq * cols * 4)
+        args = (n, c, h, w_, oc, 3, 3, 1, 1, 1, 1, seq, d, proj if proj else 0, per_image)
+        pwp = dpw.ptr if dpw is not None else None
+        gpu.check(L.lcConvAttentionNchw(bufs["x"].ptr, bufs["w"].ptr, bufs["b"].ptr, pwp, out_a.ptr, *args, None, None),
+                  "lcConvAttentionNchw")
+        gpu.check(L.lcDeviceSynchronize())
+        want = out_a.download((units, seq, cols), np.float32)
+        for _ in range(2):  # two calls in a row on the shared scratch
+            gpu.check(fn(bufs["x"].ptr, bufs["w"].ptr, bufs["b"].ptr, pwp, out_b.ptr, *args, None),
+                      "lcConvAttentionNchwNoAlloc")
+            gpu.check(L.lcDeviceSynchronize())
+            got = out_b.download((units, seq, cols), np.float32)
+            close_enough(want, got, *F32_TOL)
+            assert np.isfinite(got).all()
+
+
+def test_no_alloc_rejects_over_scratch_limit(gpu):
+    fn = _bind(gpu)
+    # 8 images x 192 ch x 112 x 112 = 19.3 Mi floats of conv output > 16 Mi floats of scratch.
+    p = C.c_void_p(16)  # never dereferenced: the size check comes first
+    rc = fn(p, p, None, None, p, 8, 64, 112, 112, 192, 3, 3, 1, 1, 1, 1, 12544, 64, 0, 1, None)
+    assert rc == gpu.LC_INVALID_VALUE
+    assert 8 * 192 * 112 * 112 > SCRATCH_FLOATS
