@@ -1,12 +1,445 @@
-// bf16 attention dispatch.  The tcgen05 flash-attention kernel lives in this file; shapes it
-// does not take run the fp32-math SIMT kernel (attention_simt.cu) -- never a CPU path.
+// Flash-attention forward on the 5th-generation tensor cores (bf16 in/out, fp32 softmax and
+// accumulation), for head_dim 64 and 128.  Replaces the reference's attention forward
+// (src/attention_cpu.cpp:38-101 arithmetic; Metal modes src/attention_metal.mm:342-576) for the
+// batched bf16 config.  Output row i = sum_j softmax_j(q_i . k_j / sqrt(d)) v_j, j <= i if causal,
+// then the optional postprocess out*scale + bias (ReLU) of src/attention.cpp:41-60.
+//
+// One CTA = one 128-row Q tile of one (batch, head) unit; 192 threads:
+//   warp 0      TMA: Q once, then K_j / V_j tiles (128 keys) into a 2-stage ring, 3-D tensor
+//               maps [units, S, D] so rows past S read as zero; 128-byte swizzle.
+//   warp 1      MMA (one thread): S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1}
+//               overlaps the softmax of S_j), then O += P_j V_j once P_j is in shared memory.
+//   warps 2..5  softmax + epilogue: each thread owns one query row (= one TMEM lane), so row
+//               max and sum need no shuffles.  Scores are scaled into the log2 domain; O is
+//               rescaled in TMEM only when the running max grows by more than 8 (2^8), which
+//               keeps exp2 values <= 256 and the final O / l exact.  P is written as bf16 in
+//               the UMMA K-major 128-byte-swizzled layout.  The epilogue divides by l, applies
+//               the postprocess and stores bf16.
+// Causal: only KV tiles at or below the diagonal are visited; per-element masks only on the
+// diagonal / sequence-tail tile.  CTAs are issued heaviest-first (largest Q tile index).
+// All mbarrier waits are bounded (common.cuh).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
 #include "common.cuh"
 #include "lc_internal.hpp"
 
 namespace lcb {
 
-bool attention_bf16_tc_supported(const AttnArgs&) { return false; }
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                       uint32_t box_rows, uint32_t box_cols);
+void* tensor_map_encoder();
 
-cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) { return attention_bf16_simt(a, s); }
+namespace {
+
+constexpr int TILE = 128;        // query rows per CTA and keys per KV tile
+constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
+constexpr int KV_STAGES = 2;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t TMEM_COLS = 512;  // S buffers at 0 and 128, O at 256
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;
+
+struct AttnTail {
+  uint64_t q_full;
+  uint64_t k_full[KV_STAGES];
+  uint64_t v_full[KV_STAGES];
+  uint64_t kv_empty[KV_STAGES];
+  uint64_t s_full[2];
+  uint64_t p_full;
+  uint64_t o_done;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int D>
+struct Layout {
+  static constexpr int NCH = D / 64;                      // 64-column chunks per row
+  static constexpr int Q_BYTES = NCH * CHUNK_BYTES;
+  static constexpr int KV_BYTES = NCH * CHUNK_BYTES;
+  static constexpr int P_BYTES = 2 * CHUNK_BYTES;          // 128 keys = 2 chunks
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;
+  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
+  static constexpr int P_OFF = V_OFF + KV_STAGES * KV_BYTES;
+  static constexpr int TAIL_OFF = P_OFF + P_BYTES;
+  static constexpr size_t SMEM = 1024 + TAIL_OFF + sizeof(AttnTail);
+};
+
+struct FaParams {
+  __nv_bfloat16* out;
+  int units, seq, nq;  // nq = Q tiles per unit
+  int causal;
+  float scale_log2;    // softmax scale * log2(e)
+  float post_scale, post_bias;
+  int post_relu, post;
+  unsigned* err_word;
+};
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast, so the warp stays
+// converged for the .sync.aligned tcgen05 loads that follow even on the abort path.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* err,
+                                          unsigned code) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, err, code) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
+// 3-D TMA load: coordinates (d, row, unit).
+__device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, int nch, int row, int unit,
+                                          uint64_t* bar) {
+  for (int c = 0; c < nch; ++c) tma_load_3d(dst + c * CHUNK_BYTES, map, c * 64, row, unit, bar);
+}
+
+template <int D>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                  const __grid_constant__ CUtensorMap map_v, const FaParams p) {
+  using LY = Layout<D>;
+  constexpr int NCH = LY::NCH;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  AttnTail* st = reinterpret_cast<AttnTail*>(smem + LY::TAIL_OFF);
+  uint8_t* sQ = smem + LY::Q_OFF;
+  uint8_t* sK = smem + LY::K_OFF;
+  uint8_t* sV = smem + LY::V_OFF;
+  uint8_t* sP = smem + LY::P_OFF;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Heaviest-first: blocks [0, units) take the last Q tile of every unit, and so on.
+  const int qt = p.nq - 1 - static_cast<int>(blockIdx.x) / p.units;
+  const int unit = static_cast<int>(blockIdx.x) % p.units;
+  const int q0 = qt * TILE;
+  const int kv_tiles_all = (p.seq + TILE - 1) / TILE;
+  const int n_kv = p.causal ? min(kv_tiles_all, qt + 1) : kv_tiles_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&st->q_full, 1);
+    for (int s = 0; s < KV_STAGES; ++s) {
+      mbar_init(&st->k_full[s], 1);
+      mbar_init(&st->v_full[s], 1);
+      mbar_init(&st->kv_empty[s], 1);
+    }
+    mbar_init(&st->s_full[0], 1);
+    mbar_init(&st->s_full[1], 1);
+    mbar_init(&st->p_full, 4);
+    mbar_init(&st->o_done, 1);
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+  }
+  if (warp == 0) {
+    tmem_alloc(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
+      load_rows(sQ, &map_q, NCH, q0, unit, &st->q_full);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % KV_STAGES;
+        const uint32_t ph = (j / KV_STAGES) & 1;
+        if (!mbar_wait_bounded(&st->kv_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&st->k_full[s], LY::KV_BYTES);
+        load_rows(sK + s * LY::KV_BYTES, &map_k, NCH, j * TILE, unit, &st->k_full[s]);
+        mbar_arrive_expect_tx(&st->v_full[s], LY::KV_BYTES);
+        load_rows(sV + s * LY::KV_BYTES, &map_v, NCH, j * TILE, unit, &st->v_full[s]);
+        ++issued;
+      }
+      if (!ok) {
+        // Let already-issued copies land before the CTA exits (bounded).
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->q_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+        for (int j = issued > KV_STAGES ? issued - KV_STAGES : 0; j < issued; ++j) {
+          const int s = j % KV_STAGES;
+          const uint32_t ph = (j / KV_STAGES) & 1;
+          const uint64_t t1 = globaltimer_ns();
+          while (!(mbar_try_wait(&st->k_full[s], ph) && mbar_try_wait(&st->v_full[s], ph)) &&
+                 globaltimer_ns() - t1 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TILE, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P K-major, V MN-major
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
+      bool issued = false;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % KV_STAGES;
+        if (!mbar_wait_bounded(&st->k_full[s], (j / KV_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
+          return false;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + s * LY::KV_BYTES);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>((j & 1) * TILE);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+          umma_f16_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+                      IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(&st->s_full[j & 1]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j % KV_STAGES;
+        if (j + 1 < n_kv && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        if (!mbar_wait_bounded(&st->p_full, j & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !mbar_wait_bounded(&st->v_full[s], (j / KV_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + s * LY::KV_BYTES);
+        const uint32_t o_tmem = tmem + 2 * TILE;
+#pragma unroll
+        for (int kk = 0; kk < TILE / 16; ++kk) {
+          // A = P (keys are K): chunk kk/4, +32 B per 16 keys.  B = V, MN-major: +16 rows*128 B.
+          const uint64_t adesc = smem_desc_sw128(p_addr + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, CHUNK_BYTES, 1024);
+          umma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&st->kv_empty[s]);
+        umma_commit(&st->o_done);
+      }
+      if (!ok && issued) {
+        umma_commit(&st->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // row within the Q tile == TMEM lane
+    const int qrow = q0 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t o_tmem = tmem + lane_base + 2 * TILE;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!warp_wait(&st->s_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[TILE];
+      {
+        const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TILE);
+#pragma unroll
+        for (int c = 0; c < TILE; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(s_tmem + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) s[c + e] = __uint_as_float(r[e]) * p.scale_log2;
+        }
+      }
+      const int kv0 = j * TILE;
+      // Keys allowed for this row: k < seq, and k <= qrow when causal.
+      const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
+      if (kv0 + TILE - 1 > kmax) {
+#pragma unroll
+        for (int e = 0; e < TILE; ++e)
+          if (kv0 + e > kmax) s[e] = -INFINITY;
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < TILE; ++e) mx = fmaxf(mx, s[e]);
+      if (j > 0) {
+        // PV_{j-1} finished: P buffer free and O stable for a rescale.
+        if (!warp_wait(&st->o_done, (j - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      const bool need = mx > m + RESCALE_THRESHOLD;
+      float factor = 1.0f;
+      if (need) {
+        factor = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
+        l *= factor;
+        m = mx;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(o_tmem + c, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
+          tmem_st16(o_tmem + c, r);
+        }
+        tmem_wait_st();
+      }
+      // m is finite here: key 0 <= qrow is always allowed, so the first tile sets it.
+      float sum = 0.0f;
+      uint8_t* prow = sP + row * 128;
+#pragma unroll
+      for (int g = 0; g < TILE / 8; ++g) {
+        float e8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          e8[e] = exp2f(s[g * 8 + e] - m);
+          sum += e8[e];
+        }
+        uint4 v;
+        v.x = pack_bf16x2(e8[0], e8[1]);
+        v.y = pack_bf16x2(e8[2], e8[3]);
+        v.z = pack_bf16x2(e8[4], e8[5]);
+        v.w = pack_bf16x2(e8[6], e8[7]);
+        const int chunk = g >> 3, gg = g & 7;
+        *reinterpret_cast<uint4*>(prow + chunk * CHUNK_BYTES + ((gg ^ (row & 7)) << 4)) = v;
+      }
+      l += sum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->p_full);
+    }
+    if (ok && warp_wait(&st->o_done, (n_kv - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      __nv_bfloat16* orow = p.out + (static_cast<long long>(unit) * p.seq + qrow) * D;
+#pragma unroll 1
+      for (int c = 0; c < D; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(o_tmem + c, r);
+        tmem_wait_ld();
+        float x[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float y = __uint_as_float(r[e]) * inv;
+          if (p.post) {
+            y = y * p.post_scale + p.post_bias;
+            if (p.post_relu && y < 0.0f) y = 0.0f;
+          }
+          x[e] = y;
+        }
+        if (qrow < p.seq) {
+          uint4 a, b;
+          a.x = pack_bf16x2(x[0], x[1]);
+          a.y = pack_bf16x2(x[2], x[3]);
+          a.z = pack_bf16x2(x[4], x[5]);
+          a.w = pack_bf16x2(x[6], x[7]);
+          b.x = pack_bf16x2(x[8], x[9]);
+          b.y = pack_bf16x2(x[10], x[11]);
+          b.z = pack_bf16x2(x[12], x[13]);
+          b.w = pack_bf16x2(x[14], x[15]);
+          reinterpret_cast<uint4*>(orow + c)[0] = a;
+          reinterpret_cast<uint4*>(orow + c)[1] = b;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// [units, seq, d] bf16, box [1, 128, 64], 128-byte swizzle, zero fill past seq.
+bool make_tmap_heads(CUtensorMap* map, const void* base, int units, int seq, int d) {
+  auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(units)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(seq) * d * 2};
+  cuuint32_t box[3] = {64, TILE, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int D>
+cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  CUtensorMap mq, mk, mv;
+  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D) ||
+      !make_tmap_heads(&mv, a.v, a.units, a.seq, D))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(Layout<D>::SMEM));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  FaParams p;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.units = a.units;
+  p.seq = a.seq;
+  p.nq = (a.seq + TILE - 1) / TILE;
+  p.causal = a.causal;
+  p.scale_log2 = a.scale * LOG2E;
+  p.post_scale = a.post_scale;
+  p.post_bias = a.post_bias;
+  p.post_relu = a.post_relu;
+  p.post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
+  p.err_word = ctx->err_word;
+  const long long blocks = static_cast<long long>(p.nq) * a.units;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D>::SMEM, s>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool attention_bf16_tc_supported(const AttnArgs& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const long long hs = static_cast<long long>(a.seq) * a.d;
+  return (a.d == 64 || a.d == 128) && a.proj_w == nullptr && a.q_unit_stride == hs && a.k_unit_stride == hs &&
+         a.v_unit_stride == hs && a.out_unit_stride == hs && al(a.q) && al(a.k) && al(a.v) && al(a.out) &&
+         tensor_map_encoder() != nullptr;
+}
+
+cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) {
+  if (attention_bf16_tc_supported(a)) return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+  return attention_bf16_simt(a, s);
+}
 
 }  // namespace lcb
