@@ -208,6 +208,13 @@ def run_ours(args, rank, world, local_rank):
         lc.check(L.lcMatMul(C.c_void_p(A.data_ptr()), C.c_void_p(Bm.data_ptr()), C.c_void_p(Cm.data_ptr()), nr, GK,
                             GN, lc.BF16, None, sp), "matmul")
 
+    if args.only:
+        fn = {"gemm": gemm, "attention": attn}[args.only]
+        for _ in range(args.warmup + args.steps):
+            fn()
+        torch.cuda.synchronize()
+        return
+
     for _ in range(args.warmup):
         attn()
         gemm()
@@ -394,6 +401,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--only", default=None, choices=["gemm", "attention"],
+                    help="run only this kernel's warm-up + timed launches (for ncu captures); prints no JSON")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
