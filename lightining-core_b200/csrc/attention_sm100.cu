@@ -5,7 +5,8 @@
 // then the optional postprocess out*scale + bias (ReLU) of src/attention.cpp:41-60.
 //
 // One CTA = one 128-row Q tile of one (batch, head) unit; 192 threads:
-//   warp 0      TMA: Q once, then K_j / V_j tiles (128 keys) into a 2-stage ring, 3-D tensor
+//   warp 0      TMA: Q once, then K_j and V_j tiles (128 keys) into two 2-stage rings (K freed
+//               once S_j is done, V once PV_j is done, so loads run ahead of the MMAs); 3-D tensor
 //               maps [units, S, D] so rows past S read as zero; 128-byte swizzle.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1}
 //               overlaps the softmax of S_j), then O += P_j V_j once P_j is in shared memory.
@@ -16,7 +17,8 @@
 //               the UMMA K-major 128-byte-swizzled layout.  The epilogue divides by l, applies
 //               the postprocess and stores bf16.
 // Causal: only KV tiles at or below the diagonal are visited; per-element masks only on the
-// diagonal / sequence-tail tile.  CTAs are issued heaviest-first (largest Q tile index).
+// diagonal / sequence-tail tile.  CTAs run unit by unit (heaviest Q tile first inside a unit), so
+// a wave of CTAs shares the K/V of few units in L2.
 // All mbarrier waits are bounded (common.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -34,11 +36,13 @@ void* tensor_map_encoder();
 
 namespace {
 
-constexpr int TILE = 128;        // query rows per CTA and keys per KV tile
+constexpr int TILE = 128;               // query rows per CTA (= TMEM lanes)
+constexpr int TK = 64;                  // keys per KV tile
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
+constexpr int KCHUNK_BYTES = TK * 128;  // one [64 rows x 64 bf16] swizzled box = 8 KB
 constexpr int KV_STAGES = 2;
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;  // S buffers at 0 and 128, O at 256
+constexpr uint32_t TMEM_COLS = 256;  // S buffers at 0 and 64, O at 128: two CTAs fit one SM
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
@@ -46,7 +50,8 @@ struct AttnTail {
   uint64_t q_full;
   uint64_t k_full[KV_STAGES];
   uint64_t v_full[KV_STAGES];
-  uint64_t kv_empty[KV_STAGES];
+  uint64_t k_empty[KV_STAGES];  // K_j consumed by S_j: refilled early, independent of PV
+  uint64_t v_empty[KV_STAGES];  // V_j consumed by PV_j
   uint64_t s_full[2];
   uint64_t p_full;
   uint64_t o_done;
@@ -59,14 +64,17 @@ template <int D>
 struct Layout {
   static constexpr int NCH = D / 64;                      // 64-column chunks per row
   static constexpr int Q_BYTES = NCH * CHUNK_BYTES;
-  static constexpr int KV_BYTES = NCH * CHUNK_BYTES;
-  static constexpr int P_BYTES = 2 * CHUNK_BYTES;          // 128 keys = 2 chunks
+  static constexpr int KV_BYTES = NCH * KCHUNK_BYTES;
+  static constexpr int P_BYTES = CHUNK_BYTES;              // 128 rows x 64 keys = 1 chunk
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
   static constexpr int P_OFF = V_OFF + KV_STAGES * KV_BYTES;
   static constexpr int TAIL_OFF = P_OFF + P_BYTES;
-  static constexpr size_t SMEM = 1024 + TAIL_OFF + sizeof(AttnTail);
+  // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel
+  // without static shared memory starts 1 KB-aligned; the kernel checks this and bails out
+  // with an error code otherwise.
+  static constexpr size_t SMEM = TAIL_OFF + sizeof(AttnTail);
 };
 
 struct FaParams {
@@ -78,6 +86,14 @@ struct FaParams {
   int post_relu, post;
   unsigned* err_word;
 };
+
+// 2^x with the hardware approximation (MUFU ex2, flush-to-zero): P is rounded to bf16 right
+// after, and results below 2^-126 are irrelevant to a softmax weight.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -94,19 +110,23 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // 3-D TMA load: coordinates (d, row, unit).
-__device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, int nch, int row, int unit,
-                                          uint64_t* bar) {
-  for (int c = 0; c < nch; ++c) tma_load_3d(dst + c * CHUNK_BYTES, map, c * 64, row, unit, bar);
+__device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, int nch, int chunk_bytes, int row,
+                                          int unit, uint64_t* bar) {
+  for (int c = 0; c < nch; ++c) tma_load_3d(dst + c * chunk_bytes, map, c * 64, row, unit, bar);
 }
 
 template <int D>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const FaParams p) {
   using LY = Layout<D>;
   constexpr int NCH = LY::NCH;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if ((smem_u32(smem_raw) & 1023u) != 0) {  // the 128-byte swizzle atoms need 1 KB alignment
+    if (threadIdx.x == 0) atomicCAS(p.err_word, 0u, static_cast<unsigned>(kErrAttnLoadWait) | 0x1000u);
+    return;
+  }
+  uint8_t* smem = smem_raw;
   AttnTail* st = reinterpret_cast<AttnTail*>(smem + LY::TAIL_OFF);
   uint8_t* sQ = smem + LY::Q_OFF;
   uint8_t* sK = smem + LY::K_OFF;
@@ -115,19 +135,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Heaviest-first: blocks [0, units) take the last Q tile of every unit, and so on.
-  const int qt = p.nq - 1 - static_cast<int>(blockIdx.x) / p.units;
-  const int unit = static_cast<int>(blockIdx.x) % p.units;
+  // Unit-major order (a wave shares the K/V of few units in L2), heaviest Q tile first inside a unit.
+  const int qt = p.nq - 1 - static_cast<int>(blockIdx.x) % p.nq;
+  const int unit = static_cast<int>(blockIdx.x) / p.nq;
   const int q0 = qt * TILE;
-  const int kv_tiles_all = (p.seq + TILE - 1) / TILE;
-  const int n_kv = p.causal ? min(kv_tiles_all, qt + 1) : kv_tiles_all;
+  const int kv_tiles_all = (p.seq + TK - 1) / TK;
+  const int n_kv = p.causal ? min(kv_tiles_all, (q0 + TILE - 1) / TK + 1) : kv_tiles_all;
 
   if (threadIdx.x == 0) {
     mbar_init(&st->q_full, 1);
     for (int s = 0; s < KV_STAGES; ++s) {
       mbar_init(&st->k_full[s], 1);
       mbar_init(&st->v_full[s], 1);
-      mbar_init(&st->kv_empty[s], 1);
+      mbar_init(&st->k_empty[s], 1);
+      mbar_init(&st->v_empty[s], 1);
     }
     mbar_init(&st->s_full[0], 1);
     mbar_init(&st->s_full[1], 1);
@@ -156,18 +177,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int issued = 0;
       bool ok = true;
       mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
-      load_rows(sQ, &map_q, NCH, q0, unit, &st->q_full);
+      load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % KV_STAGES;
         const uint32_t ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait_bounded(&st->kv_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
+        if (!mbar_wait_bounded(&st->k_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
           ok = false;
           break;
         }
         mbar_arrive_expect_tx(&st->k_full[s], LY::KV_BYTES);
-        load_rows(sK + s * LY::KV_BYTES, &map_k, NCH, j * TILE, unit, &st->k_full[s]);
+        load_rows(sK + s * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[s]);
+        if (!mbar_wait_bounded(&st->v_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          ++issued;  // K_j is in flight: drain it below
+          break;
+        }
         mbar_arrive_expect_tx(&st->v_full[s], LY::KV_BYTES);
-        load_rows(sV + s * LY::KV_BYTES, &map_v, NCH, j * TILE, unit, &st->v_full[s]);
+        load_rows(sV + s * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[s]);
         ++issued;
       }
       if (!ok) {
@@ -188,7 +214,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TILE, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TK, 0, 0);    // Q K-major, K K-major
       constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P K-major, V MN-major
       const uint32_t q_addr = smem_u32(sQ);
       const uint32_t p_addr = smem_u32(sP);
@@ -200,15 +226,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sK + s * LY::KV_BYTES);
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>((j & 1) * TILE);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>((j & 1) * TK);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          umma_f16_ss(d_tmem, smem_desc_sw128(q_addr + off, 16, 1024), smem_desc_sw128(k_addr + off, 16, 1024),
+          const uint32_t qoff = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * KCHUNK_BYTES + (kk & 3) * 32;
+          umma_f16_ss(d_tmem, smem_desc_sw128(q_addr + qoff, 16, 1024), smem_desc_sw128(k_addr + koff, 16, 1024),
                       IDESC_S, kk > 0 ? 1u : 0u);
         }
         issued = true;
         umma_commit(&st->s_full[j & 1]);
+        umma_commit(&st->k_empty[s]);
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -225,15 +253,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + s * LY::KV_BYTES);
-        const uint32_t o_tmem = tmem + 2 * TILE;
+        const uint32_t o_tmem = tmem + 2 * TK;
 #pragma unroll
-        for (int kk = 0; kk < TILE / 16; ++kk) {
-          // A = P (keys are K): chunk kk/4, +32 B per 16 keys.  B = V, MN-major: +16 rows*128 B.
-          const uint64_t adesc = smem_desc_sw128(p_addr + (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, CHUNK_BYTES, 1024);
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          // A = P (keys are K): +32 B per 16 keys.  B = V, MN-major: 64-column d chunks 8 KB apart
+          // (LBO), +16 key rows * 128 B per step.
+          const uint64_t adesc = smem_desc_sw128(p_addr + kk * 32, 16, 1024);
+          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, KCHUNK_BYTES, 1024);
           umma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&st->kv_empty[s]);
+        umma_commit(&st->v_empty[s]);
         umma_commit(&st->o_done);
       }
       if (!ok && issued) {
@@ -249,7 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int row = quarter * 32 + lane;  // row within the Q tile == TMEM lane
     const int qrow = q0 + row;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t o_tmem = tmem + lane_base + 2 * TILE;
+    const uint32_t o_tmem = tmem + lane_base + 2 * TK;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
@@ -258,29 +287,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         break;
       }
       tc_fence_after();
-      float s[TILE];
+      // Both 32-column score loads in flight before a single wait.
+      uint32_t r[TK / 32][32];
       {
-        const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TILE);
+        const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TK);
 #pragma unroll
-        for (int c = 0; c < TILE; c += 32) {
-          uint32_t r[32];
-          tmem_ld32(s_tmem + c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) s[c + e] = __uint_as_float(r[e]) * p.scale_log2;
-        }
+        for (int c = 0; c < TK / 32; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
+        tmem_wait_ld();
       }
-      const int kv0 = j * TILE;
+      const int kv0 = j * TK;
       // Keys allowed for this row: k < seq, and k <= qrow when causal.
       const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
-      if (kv0 + TILE - 1 > kmax) {
+      if (kv0 + TK - 1 > kmax) {
 #pragma unroll
-        for (int e = 0; e < TILE; ++e)
-          if (kv0 + e > kmax) s[e] = -INFINITY;
+        for (int e = 0; e < TK; ++e)
+          if (kv0 + e > kmax) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // Row max with 8 independent partial maxima (short dependency chains), in raw score units;
+      // scale > 0 so max(s)*scale == max(s*scale).
+      float pm[8];
 #pragma unroll
-      for (int e = 0; e < TILE; ++e) mx = fmaxf(mx, s[e]);
+      for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(r[0][a]);
+#pragma unroll
+      for (int e = 8; e < TK; ++e) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(r[e >> 5][e & 31]));
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * p.scale_log2;
       if (j > 0) {
         // PV_{j-1} finished: P buffer free and O stable for a rescale.
         if (!warp_wait(&st->o_done, (j - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
@@ -299,34 +330,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (j > 0 && __any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < D; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(o_tmem + c, r);
+          uint32_t o[16];
+          tmem_ld16(o_tmem + c, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * factor);
-          tmem_st16(o_tmem + c, r);
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          tmem_st16(o_tmem + c, o);
         }
         tmem_wait_st();
       }
-      // m is finite here: key 0 <= qrow is always allowed, so the first tile sets it.
-      float sum = 0.0f;
+      // p = exp2(s*scale - m), one FFMA + ex2 each; m is finite here (key 0 <= qrow is always
+      // visible, so the first tile sets it).  8 partial sums keep the adds independent.
+      const float sc = p.scale_log2, neg_m = -m;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint8_t* prow = sP + row * 128;
 #pragma unroll
-      for (int g = 0; g < TILE / 8; ++g) {
+      for (int g = 0; g < TK / 8; ++g) {
         float e8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          e8[e] = exp2f(s[g * 8 + e] - m);
-          sum += e8[e];
+          e8[e] = fast_exp2(fmaf(__uint_as_float(r[(g * 8 + e) >> 5][(g * 8 + e) & 31]), sc, neg_m));
+          ps[e] += e8[e];
         }
         uint4 v;
         v.x = pack_bf16x2(e8[0], e8[1]);
         v.y = pack_bf16x2(e8[2], e8[3]);
         v.z = pack_bf16x2(e8[4], e8[5]);
         v.w = pack_bf16x2(e8[6], e8[7]);
-        const int chunk = g >> 3, gg = g & 7;
-        *reinterpret_cast<uint4*>(prow + chunk * CHUNK_BYTES + ((gg ^ (row & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = v;
       }
+      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
@@ -382,12 +415,12 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 // [units, seq, d] bf16, box [1, 128, 64], 128-byte swizzle, zero fill past seq.
-bool make_tmap_heads(CUtensorMap* map, const void* base, int units, int seq, int d) {
+bool make_tmap_heads(CUtensorMap* map, const void* base, int units, int seq, int d, int box_rows) {
   auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return false;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(units)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * 2, static_cast<cuuint64_t>(seq) * d * 2};
-  cuuint32_t box[3] = {64, TILE, 1};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -399,13 +432,15 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
   CUtensorMap mq, mk, mv;
-  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D) ||
-      !make_tmap_heads(&mv, a.v, a.units, a.seq, D))
+  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D, TILE) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D, TK) ||
+      !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TK))
     return cudaErrorInvalidValue;
   static bool attr_set = false;  // benign race: idempotent
   if (!attr_set) {
     cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(Layout<D>::SMEM));
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }

@@ -19,7 +19,7 @@ import os
 import numpy as np
 
 _PKG_ROOT = os.path.abspath(os.path.join(os.path.dirname(__file__), "..", ".."))
-LIB_PATH = os.path.join(_PKG_ROOT, "liblc_b200.so")
+LIB_PATH = os.environ.get("LC_B200_LIB") or os.path.join(_PKG_ROOT, "liblc_b200.so")
 
 if not os.path.exists(LIB_PATH):
     raise ImportError(f"{LIB_PATH} is not built; run `make -C {_PKG_ROOT}`")
