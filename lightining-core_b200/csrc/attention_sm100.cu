@@ -40,7 +40,9 @@ constexpr int TILE = 128;               // query rows per CTA (= TMEM lanes)
 constexpr int TK = 64;                  // keys per KV tile
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
 constexpr int KCHUNK_BYTES = TK * 128;  // one [64 rows x 64 bf16] swizzled box = 8 KB
-constexpr int KV_STAGES = 2;
+constexpr int K_STAGES = 1;   // K_{j+1} refills as soon as S_j is done: ~a softmax of slack
+constexpr int V_STAGES = 2;   // V_{j+1} refills once PV_{j-1} is done
+constexpr int P_BUFS = 2;     // P_j goes to buffer j%2, so softmax j never waits for PV_{j-1}
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t TMEM_COLS = 256;  // S buffers at 0 and 64, O at 128: two CTAs fit one SM
 constexpr float LOG2E = 1.4426950408889634f;
@@ -48,13 +50,13 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 
 struct AttnTail {
   uint64_t q_full;
-  uint64_t k_full[KV_STAGES];
-  uint64_t v_full[KV_STAGES];
-  uint64_t k_empty[KV_STAGES];  // K_j consumed by S_j: refilled early, independent of PV
-  uint64_t v_empty[KV_STAGES];  // V_j consumed by PV_j
+  uint64_t k_full[K_STAGES];
+  uint64_t v_full[V_STAGES];
+  uint64_t k_empty[K_STAGES];  // K_j consumed by S_j: refilled early, independent of PV
+  uint64_t v_empty[V_STAGES];  // V_j consumed by PV_j
   uint64_t s_full[2];
   uint64_t p_full;
-  uint64_t o_done;
+  uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -68,9 +70,9 @@ struct Layout {
   static constexpr int P_BYTES = CHUNK_BYTES;              // 128 rows x 64 keys = 1 chunk
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
-  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_BYTES;
-  static constexpr int P_OFF = V_OFF + KV_STAGES * KV_BYTES;
-  static constexpr int TAIL_OFF = P_OFF + P_BYTES;
+  static constexpr int V_OFF = K_OFF + K_STAGES * KV_BYTES;
+  static constexpr int P_OFF = V_OFF + V_STAGES * KV_BYTES;
+  static constexpr int TAIL_OFF = P_OFF + P_BUFS * P_BYTES;
   // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel
   // without static shared memory starts 1 KB-aligned; the kernel checks this and bails out
   // with an error code otherwise.
@@ -93,6 +95,31 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32x2 arithmetic and the 3-input max of sm_100: half the FP instructions per score.
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpk2(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -144,16 +171,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(&st->q_full, 1);
-    for (int s = 0; s < KV_STAGES; ++s) {
+    for (int s = 0; s < K_STAGES; ++s) {
       mbar_init(&st->k_full[s], 1);
-      mbar_init(&st->v_full[s], 1);
       mbar_init(&st->k_empty[s], 1);
+    }
+    for (int s = 0; s < V_STAGES; ++s) {
+      mbar_init(&st->v_full[s], 1);
       mbar_init(&st->v_empty[s], 1);
     }
     mbar_init(&st->s_full[0], 1);
     mbar_init(&st->s_full[1], 1);
     mbar_init(&st->p_full, 4);
-    mbar_init(&st->o_done, 1);
+    mbar_init(&st->o_done[0], 1);
+    mbar_init(&st->o_done[1], 1);
     mbar_init(&st->drain, 1);
     st->abort_flag = 0;
     fence_barrier_init();
@@ -178,22 +208,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       bool ok = true;
       mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
       load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
+      int k_issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int s = j % KV_STAGES;
-        const uint32_t ph = (j / KV_STAGES) & 1;
-        if (!mbar_wait_bounded(&st->k_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
+        const int ks = j % K_STAGES, vs = j % V_STAGES;
+        if (j + 1 < n_kv) {  // warm L2 for the next K/V tiles while this one waits for its slot
+          for (int c = 0; c < NCH; ++c) {
+            tma_prefetch_l2_3d(&map_k, c * 64, (j + 1) * TK, unit);
+            tma_prefetch_l2_3d(&map_v, c * 64, (j + 1) * TK, unit);
+          }
+        }
+        if (!mbar_wait_bounded(&st->k_empty[ks], ((j / K_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
+                               kErrAttnLoadWait)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&st->k_full[s], LY::KV_BYTES);
-        load_rows(sK + s * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[s]);
-        if (!mbar_wait_bounded(&st->v_empty[s], ph ^ 1u, abort_flag, p.err_word, kErrAttnLoadWait)) {
+        mbar_arrive_expect_tx(&st->k_full[ks], LY::KV_BYTES);
+        load_rows(sK + ks * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[ks]);
+        ++k_issued;
+        if (!mbar_wait_bounded(&st->v_empty[vs], ((j / V_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
+                               kErrAttnLoadWait)) {
           ok = false;
-          ++issued;  // K_j is in flight: drain it below
           break;
         }
-        mbar_arrive_expect_tx(&st->v_full[s], LY::KV_BYTES);
-        load_rows(sV + s * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[s]);
+        mbar_arrive_expect_tx(&st->v_full[vs], LY::KV_BYTES);
+        load_rows(sV + vs * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[vs]);
         ++issued;
       }
       if (!ok) {
@@ -201,14 +239,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->q_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
-        for (int j = issued > KV_STAGES ? issued - KV_STAGES : 0; j < issued; ++j) {
-          const int s = j % KV_STAGES;
-          const uint32_t ph = (j / KV_STAGES) & 1;
+        auto drain = [](uint64_t* bar, uint32_t ph) {
           const uint64_t t1 = globaltimer_ns();
-          while (!(mbar_try_wait(&st->k_full[s], ph) && mbar_try_wait(&st->v_full[s], ph)) &&
-                 globaltimer_ns() - t1 < 100000000ull) {
+          while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t1 < 100000000ull) {
           }
-        }
+        };
+        for (int j = k_issued > K_STAGES ? k_issued - K_STAGES : 0; j < k_issued; ++j)
+          drain(&st->k_full[j % K_STAGES], (j / K_STAGES) & 1);
+        for (int j = issued > V_STAGES ? issued - V_STAGES : 0; j < issued; ++j)
+          drain(&st->v_full[j % V_STAGES], (j / V_STAGES) & 1);
       }
     }
   } else if (warp == 1) {
@@ -221,8 +260,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
-        const int s = j % KV_STAGES;
-        if (!mbar_wait_bounded(&st->k_full[s], (j / KV_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
+        const int s = j % K_STAGES;
+        if (!mbar_wait_bounded(&st->k_full[s], (j / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
           return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(sK + s * LY::KV_BYTES);
@@ -241,13 +280,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % KV_STAGES;
+        const int s = j % V_STAGES;
         if (j + 1 < n_kv && !issue_s(j + 1)) {
           ok = false;
           break;
         }
         if (!mbar_wait_bounded(&st->p_full, j & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !mbar_wait_bounded(&st->v_full[s], (j / KV_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
+            !mbar_wait_bounded(&st->v_full[s], (j / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
           ok = false;
           break;
         }
@@ -258,12 +297,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         for (int kk = 0; kk < TK / 16; ++kk) {
           // A = P (keys are K): +32 B per 16 keys.  B = V, MN-major: 64-column d chunks 8 KB apart
           // (LBO), +16 key rows * 128 B per step.
-          const uint64_t adesc = smem_desc_sw128(p_addr + kk * 32, 16, 1024);
+          const uint64_t adesc = smem_desc_sw128(p_addr + (j % P_BUFS) * LY::P_BYTES + kk * 32, 16, 1024);
           const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, KCHUNK_BYTES, 1024);
           umma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&st->v_empty[s]);
-        umma_commit(&st->o_done);
+        umma_commit(&st->o_done[j % P_BUFS]);
       }
       if (!ok && issued) {
         umma_commit(&st->drain);
@@ -303,22 +342,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         for (int e = 0; e < TK; ++e)
           if (kv0 + e > kmax) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
       }
-      // Row max with 8 independent partial maxima (short dependency chains), in raw score units;
-      // scale > 0 so max(s)*scale == max(s*scale).
+      // Row max: 8 independent partial maxima fed two scores per 3-input max, in raw score
+      // units (scale > 0, so max(s)*scale == max(s*scale)).
       float pm[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(r[0][a]);
 #pragma unroll
-      for (int e = 8; e < TK; ++e) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(r[e >> 5][e & 31]));
-      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * p.scale_log2;
-      if (j > 0) {
-        // PV_{j-1} finished: P buffer free and O stable for a rescale.
-        if (!warp_wait(&st->o_done, (j - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+      for (int e = 8; e < TK; e += 2)
+        pm[(e >> 1) & 7] = max3(pm[(e >> 1) & 7], __uint_as_float(r[e >> 5][e & 31]),
+                                __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31]));
+      const float mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
+                       p.scale_log2;
+      // P buffer j%2 was last read by PV_{j-2}.  o_done[j%2] completes once per use of that buffer
+      // and PV_j cannot complete before P_j exists, so this parity wait is unambiguous.
+      if (j >= 2) {
+        if (!warp_wait(&st->o_done[j % P_BUFS], ((j - 2) >> 1) & 1, abort_flag, p.err_word,
+                       kErrAttnCorrectionWait)) {
           ok = false;
           break;
         }
-        tc_fence_after();
       }
       const bool need = mx > m + RESCALE_THRESHOLD;
       float factor = 1.0f;
@@ -328,6 +370,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         m = mx;
       }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O is rescaled in place: PV_{j-1} must have landed first.
+        if (!warp_wait(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag, p.err_word,
+                       kErrAttnCorrectionWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < D; c += 16) {
           uint32_t o[16];
@@ -341,32 +390,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       }
       // p = exp2(s*scale - m), one FFMA + ex2 each; m is finite here (key 0 <= qrow is always
       // visible, so the first tile sets it).  8 partial sums keep the adds independent.
-      const float sc = p.scale_log2, neg_m = -m;
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = sP + row * 128;
+      const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
+      uint64_t ps2[4] = {0, 0, 0, 0};  // 4 independent packed partial sums
+      uint8_t* prow = sP + (j % P_BUFS) * Layout<D>::P_BYTES + row * 128;
 #pragma unroll
       for (int g = 0; g < TK / 8; ++g) {
-        float e8[8];
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          e8[e] = fast_exp2(fmaf(__uint_as_float(r[(g * 8 + e) >> 5][(g * 8 + e) & 31]), sc, neg_m));
-          ps[e] += e8[e];
+        for (int i = 0; i < 4; ++i) {
+          const int e = g * 8 + 2 * i;
+          // x = s*scale - m for two scores at once; masked scores are -inf, so ex2 gives 0.
+          float x0, x1;
+          unpk2(fma2(pk2(__uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31])),
+                     sc2, nm2),
+                x0, x1);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+          ps2[i] = add2(ps2[i], pk2(e0, e1));
+          w[i] = pack_bf16x2(e0, e1);
         }
-        uint4 v;
-        v.x = pack_bf16x2(e8[0], e8[1]);
-        v.y = pack_bf16x2(e8[2], e8[3]);
-        v.z = pack_bf16x2(e8[4], e8[5]);
-        v.w = pack_bf16x2(e8[6], e8[7]);
-        *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      const float sum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      float sum;
+      {
+        const uint64_t t = add2(add2(ps2[0], ps2[1]), add2(ps2[2], ps2[3]));
+        float a, b;
+        unpk2(t, a, b);
+        sum = a + b;
+      }
       l += sum;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&st->p_full);
     }
-    if (ok && warp_wait(&st->o_done, (n_kv - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+    // The last two PVs (one per P buffer) must have landed in O.
+    if (ok && n_kv >= 2)
+      ok = warp_wait(&st->o_done[(n_kv - 2) % P_BUFS], ((n_kv - 2) >> 1) & 1, abort_flag, p.err_word,
+                     kErrAttnCorrectionWait);
+    if (ok && warp_wait(&st->o_done[(n_kv - 1) % P_BUFS], ((n_kv - 1) >> 1) & 1, abort_flag, p.err_word,
+                        kErrAttnCorrectionWait)) {
       tc_fence_after();
       const float inv = 1.0f / l;
       __nv_bfloat16* orow = p.out + (static_cast<long long>(unit) * p.seq + qrow) * D;
