@@ -22,11 +22,16 @@ import argparse
 import ctypes as C
 import json
 import os
-import subprocess
 import sys
 import time
 
 import numpy as np
+
+_JSON_FD = 1
+
+
+def emit(line: dict) -> None:
+    os.write(_JSON_FD, (json.dumps(line) + "\n").encode())
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
@@ -64,56 +69,61 @@ def profile_traffic(name):
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region (the profiling recipe's clocks line)."""
+    """SM clock and throttle reasons sampled during the timed region.
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    Polls NVML every 10 ms from a thread (reading only; nothing is set), so even a short timed
+    region gets samples; falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, index):
         self.index = index
-        self.proc = None
-        self.path = os.path.join("/tmp", f"lc_clocks_{os.getpid()}.csv")
+        self.samples = []
+        self.reasons = set()
+        self.smax = None
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
+        import threading
+
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
-                                         stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - sampling is best effort
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    mask = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for name, bit in self.REASONS.items():
+                        if mask & bit:
+                            self.reasons.add(name)
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(0.01)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.f.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        os.unlink(self.path)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "samples": len(sm),
-                "reasons": sorted(reasons)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.smax, "samples": 0, "reasons": ["no samples"]}
+        return {"sm_mhz": float(np.median(self.samples)), "sm_max_mhz": self.smax, "samples": len(self.samples),
+                "reasons": sorted(self.reasons), "source": "NVML, 10 ms polling during the timed steps"}
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -158,7 +168,7 @@ def run_reference(args, rank):
             "config": dict(CONFIG, parallelism=f"cpu threads x{threads} (bounded sample of the workload)"),
             "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": threads, "kind": kind, "sample": desc},
             "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 CONFIG = {"workload": "cfg3 causal attention bf16 [8,16,2048,128] + cfg4 matmul2d bf16 8192^3 (fp32 accumulate)",
@@ -181,10 +191,10 @@ def run_ours(args, rank, world, local_rank):
     L = lc.lib
 
     # ---- shards: units [u0, u1) of attention, rows [r0, r1) of the GEMM
-    per_u = UNITS // world
-    u0, u1 = rank * per_u, (rank + 1) * per_u
-    per_r = GM // world
-    r0, r1 = rank * per_r, (rank + 1) * per_r
+    from lightning_core_b200.sharding import assemble, shard_range
+
+    u0, u1 = shard_range(UNITS, rank, world)
+    r0, r1 = shard_range(GM, rank, world)
     nu, nr = u1 - u0, r1 - r0
 
     g = torch.Generator(device=dev)
@@ -249,17 +259,15 @@ def run_ours(args, rank, world, local_rank):
     # ---- assembling all-gather (outside the compute timing)
     assemble_ms = None
     if world > 1:
-        full_attn = torch.empty((world * nu, S, D), device=dev, dtype=torch.bfloat16)
-        full_c = torch.empty((world * nr, GN), device=dev, dtype=torch.bfloat16)
         for _ in range(2):
-            dist.all_gather_into_tensor(full_attn, attn_out)
-            dist.all_gather_into_tensor(full_c, Cm)
+            assemble(attn_out, UNITS, rank, world)
+            assemble(Cm, GM, rank, world)
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        dist.all_gather_into_tensor(full_attn, attn_out)
-        dist.all_gather_into_tensor(full_c, Cm)
+        full_attn = assemble(attn_out, UNITS, rank, world)
+        full_c = assemble(Cm, GM, rank, world)
         e1.record(stream)
         torch.cuda.synchronize()
         am = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
@@ -303,7 +311,7 @@ def run_ours(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "extras": extras,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def e2e_run(args, lc, torch, q, k, v, A, Bm, nu, nr, world, dev):
@@ -398,12 +406,16 @@ def extra_configs(args, lc, torch, dev, sp):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--only", default=None, choices=["gemm", "attention"],
                     help="run only this kernel's warm-up + timed launches (for ncu captures); prints no JSON")
     args = ap.parse_args()
+    # Libraries (NCCL's version banner, ...) may write to fd 1; keep it for the one JSON line only.
+    global _JSON_FD
+    _JSON_FD = os.dup(1)
+    os.dup2(2, 1)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
