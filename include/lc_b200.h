@@ -251,6 +251,28 @@ lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataT
  * (the reference's LN formula, README.md:2267-2270).  Device pointers, fp32. */
 lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, float eps, lcStream_t stream);
 
+/* ---- per-shape auto-tune cache (src/ops/matmul_metal.mm:416-577, src/attention_metal.mm:184-336) */
+/* CSV `#lc_tune_cache,<matmul|attention>,2` + `#columns,...`; keys (m,k,n,dtype) for matmul and
+ * (seq,head_dim,causal,dtype) for attention; values are sm_100a kernel configuration names
+ * ("simt128x128", "simt128x64", "simt64x64", "tcgen05_128x256", "simt", "tcgen05").  A NULL path
+ * means CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE, which is also loaded on first use and
+ * rewritten whenever an entry is added.  Load rejects a file with an unknown header
+ * (LC_NOT_SUPPORTED) and keeps the current rows. */
+typedef enum lcTuneKind { LC_TUNE_MATMUL = 0, LC_TUNE_ATTENTION = 1 } lcTuneKind;
+lcError_t lcTuneCacheLoad(lcTuneKind kind, const char* path);
+lcError_t lcTuneCacheSave(lcTuneKind kind, const char* path);
+/* Clears the cache (the reference's matMulMetalResetTuning, src/ops/matmul_metal.mm:1803-1834). */
+lcError_t lcTuneCacheReset(lcTuneKind kind);
+size_t lcTuneCacheSize(lcTuneKind kind);
+lcError_t lcTuneCacheGet(lcTuneKind kind, size_t d0, size_t d1, size_t d2, lcDataType dtype, char* config,
+                         size_t cap);
+lcError_t lcTuneCacheSet(lcTuneKind kind, size_t d0, size_t d1, size_t d2, lcDataType dtype, const char* config);
+/* Times every configuration that can run the shape on the given device buffers (1 warm-up +
+ * median of 5, CUDA events; like autoTuneTile, src/ops/matmul_metal.mm:1643-1790), stores the
+ * fastest and writes its name to `best`.  Synchronizes `stream`. */
+lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
+                           lcStream_t stream, char* best, size_t cap);
+
 /* ---- device error word: kernels' bounded waits record where they gave up ---------------- */
 /* Returns LC_DRIVER_ERROR and the recorded code if any kernel on the current device gave up a
  * bounded wait since the last clear; LC_SUCCESS otherwise.  Synchronizes the device. */

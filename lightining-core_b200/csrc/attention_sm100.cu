@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include "../../include/lc_b200.h"
 #include "common.cuh"
 #include "lc_internal.hpp"
 
@@ -535,7 +536,10 @@ bool attention_bf16_tc_supported(const AttnArgs& a) {
 }
 
 cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) {
-  if (attention_bf16_tc_supported(a)) return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+  std::string cfg;
+  const bool forced_simt =
+      tune_lookup(LC_TUNE_ATTENTION, a.seq, a.d, a.causal, LC_DTYPE_BF16, &cfg) && cfg == "simt";
+  if (!forced_simt && attention_bf16_tc_supported(a)) return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
   return attention_bf16_simt(a, s);
 }
 

@@ -4,20 +4,23 @@
 // it) rules out plain TF32 tensor cores, so these kernels accumulate with fp32 FFMA in k order,
 // exactly the reduction order of the reference's i-p-j loop for each output element.
 //
-// Tiling: 128x128 output tile per 256-thread CTA, BK = 8, double-buffered shared memory, each
-// thread owns an 8x8 sub-tile split into two 4-row x two 4-column strips (rows ty*4 and
-// ty*4+64, cols tx*4 and tx*4+64) so the float4 shared-memory reads are conflict-free.
+// Tiling: three CTA tiles (128x128 with 8x8 per thread, 128x64 with 8x8, 64x64 with 4x4), BK = 8,
+// double-buffered shared memory; thread tiles are split into 4-wide strips so every
+// shared-memory read is a conflict-free float4.  The tile comes from the auto-tune cache when it
+// has an entry for the shape, else the largest tile that still gives every SM a CTA.
 // The operands come from loader functors: dense row-major for matmul, an on-the-fly im2col
 // gather (B side) for conv (the im2col matrix is never materialised); the epilogue functor writes
 // row-major for matmul or NCHW (+bias, ReLU) for conv.
 #include <cuda_bf16.h>
+
+#include <cstring>
 
 #include "lc_internal.hpp"
 
 namespace lcb {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 8, NT = 256;
+constexpr int BK = 8;
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v) { return static_cast<float>(v); }
@@ -90,37 +93,42 @@ struct NchwEpi {
   }
 };
 
-template <class LA, class LB, class Epi>
-__global__ void __launch_bounds__(NT) simt_gemm_kernel(LA la, LB lb, Epi epi, int M, int N, int K) {
+// Tile BM x BN per CTA, thread tile TM x TN (multiples of 4, split into 4-wide strips spaced
+// BM/(TM/4) rows and BN/(TN/4) columns so every shared-memory read is a conflict-free float4).
+template <int BM, int BN, int TM, int TN, class LA, class LB, class Epi>
+__global__ void __launch_bounds__((BM / TM) * (BN / TN))
+    simt_gemm_kernel(LA la, LB lb, Epi epi, int M, int N, int K) {
+  constexpr int TX = BN / TN, TY = BM / TM, NT = TX * TY;
+  constexpr int RS = BM / (TM / 4), CS = BN / (TN / 4);  // strip spacing
+  constexpr int AE = BM * BK / NT, BE = BK * BN / NT;    // elements each thread stages
+  static_assert(TM % 4 == 0 && TN % 4 == 0 && BK % AE == 0 && BN % BE == 0 && AE >= 1 && BE >= 1, "tile");
   __shared__ __align__(16) float As[2][BK][BM];
   __shared__ __align__(16) float Bs[2][BK][BN];
   const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
+  const int tx = tid % TX, ty = tid / TX;
   const int row0 = blockIdx.y * BM, col0 = blockIdx.x * BN;
+  const int a_r = tid / (BK / AE), a_k = (tid % (BK / AE)) * AE;   // AE consecutive k of one A row
+  const int b_k = tid / (BN / BE), b_c = (tid % (BN / BE)) * BE;   // BE consecutive cols of one B row
 
-  // Loader assignment: A tile 128x8 -> thread loads row (tid>>1), k (tid&1)*4 .. +3.
-  const int a_r = tid >> 1, a_k = (tid & 1) * 4;
-  // B tile 8x128 -> thread loads k (tid>>5), cols (tid&31)*4 .. +3.
-  const int b_k = tid >> 5, b_c = (tid & 31) * 4;
-
-  float ra[4], rb[4];
+  float ra[AE], rb[BE];
   auto gload = [&](int k0) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) ra[i] = la(row0 + a_r, k0 + a_k + i);
+    for (int i = 0; i < AE; ++i) ra[i] = la(row0 + a_r, k0 + a_k + i);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) rb[i] = lb(k0 + b_k, col0 + b_c + i);
+    for (int i = 0; i < BE; ++i) rb[i] = lb(k0 + b_k, col0 + b_c + i);
   };
   auto sstore = [&](int buf) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) As[buf][a_k + i][a_r] = ra[i];
-    *reinterpret_cast<float4*>(&Bs[buf][b_k][b_c]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+    for (int i = 0; i < AE; ++i) As[buf][a_k + i][a_r] = ra[i];
+#pragma unroll
+    for (int i = 0; i < BE; ++i) Bs[buf][b_k][b_c + i] = rb[i];
   };
 
-  float acc[8][8];
+  float acc[TM][TN];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < TM; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
   const int ktiles = (K + BK - 1) / BK;
   gload(0);
@@ -131,16 +139,21 @@ __global__ void __launch_bounds__(NT) simt_gemm_kernel(LA la, LB lb, Epi epi, in
     if (kt + 1 < ktiles) gload((kt + 1) * BK);
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + 64]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + 64]);
-      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+      float av[TM], bv[TN];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
+      for (int g = 0; g < TM / 4; ++g) {
+        const float4 a4 = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4 + g * RS]);
+        av[g * 4 + 0] = a4.x; av[g * 4 + 1] = a4.y; av[g * 4 + 2] = a4.z; av[g * 4 + 3] = a4.w;
+      }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+      for (int g = 0; g < TN / 4; ++g) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4 + g * CS]);
+        bv[g * 4 + 0] = b4.x; bv[g * 4 + 1] = b4.y; bv[g * 4 + 2] = b4.z; bv[g * 4 + 3] = b4.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
     if (kt + 1 < ktiles) {
       sstore(buf ^ 1);
@@ -148,22 +161,47 @@ __global__ void __launch_bounds__(NT) simt_gemm_kernel(LA la, LB lb, Epi epi, in
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int r = row0 + ty * 4 + (i & 3) + (i >> 2) * 64;
+  for (int i = 0; i < TM; ++i) {
+    const int r = row0 + ty * 4 + (i & 3) + (i >> 2) * RS;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int c = col0 + tx * 4 + (j & 3) + (j >> 2) * 64;
+    for (int j = 0; j < TN; ++j) {
+      const int c = col0 + tx * 4 + (j & 3) + (j >> 2) * CS;
       epi(r, c, acc[i][j]);
     }
   }
 }
 
-template <class LA, class LB, class Epi>
-cudaError_t run(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s) {
+template <int BM, int BN, int TM, int TN, class LA, class LB, class Epi>
+cudaError_t run_tile(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s) {
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-  simt_gemm_kernel<<<grid, NT, 0, s>>>(la, lb, epi, M, N, K);
+  simt_gemm_kernel<BM, BN, TM, TN><<<grid, (BM / TM) * (BN / TN), 0, s>>>(la, lb, epi, M, N, K);
   return cudaGetLastError();
+}
+
+// Tile configurations (the names are the values stored in the auto-tune cache).
+enum SimtTile { kSimt128x128 = 0, kSimt128x64, kSimt64x64, kSimtTileCount };
+const char* const kSimtTileNames[kSimtTileCount] = {"simt128x128", "simt128x64", "simt64x64"};
+
+// Without a cache entry: the largest tile that still gives every SM a CTA.
+int default_simt_tile(int M, int N) {
+  const DeviceCtx* c = device_ctx();
+  const long long sms = c ? c->sm_count : 148;
+  const long long big = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
+  if (big >= sms) return kSimt128x128;
+  const long long mid = static_cast<long long>((M + 127) / 128) * ((N + 63) / 64);
+  if (mid >= sms) return kSimt128x64;
+  return kSimt64x64;
+}
+
+template <class LA, class LB, class Epi>
+cudaError_t run(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s, int tile = -1) {
+  if (tile < 0) tile = default_simt_tile(M, N);
+  switch (tile) {
+    case kSimt128x64: return run_tile<128, 64, 8, 8>(la, lb, epi, M, N, K, s);
+    case kSimt64x64: return run_tile<64, 64, 4, 4>(la, lb, epi, M, N, K, s);
+    default: return run_tile<128, 128, 8, 8>(la, lb, epi, M, N, K, s);
+  }
 }
 
 __global__ void repeat_fill_kernel(const float* src, size_t have, float* dst, size_t total) {
@@ -174,8 +212,16 @@ __global__ void repeat_fill_kernel(const float* src, size_t have, float* dst, si
 
 }  // namespace
 
-cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
-  return run(DenseA<float>{a, m, k}, DenseB<float>{b, k, n}, RowMajorEpi<float>{c, m, n}, m, n, k, s);
+cudaError_t gemm_f32_tile(const float* a, const float* b, float* c, int m, int k, int n, int tile, cudaStream_t s) {
+  return run(DenseA<float>{a, m, k}, DenseB<float>{b, k, n}, RowMajorEpi<float>{c, m, n}, m, n, k, s, tile);
+}
+
+int simt_tile_count() { return kSimtTileCount; }
+const char* simt_tile_name(int t) { return (t >= 0 && t < kSimtTileCount) ? kSimtTileNames[t] : "?"; }
+int simt_tile_from_name(const char* name) {
+  for (int t = 0; t < kSimtTileCount; ++t)
+    if (std::strcmp(name, kSimtTileNames[t]) == 0) return t;
+  return -1;
 }
 
 cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,

@@ -21,6 +21,7 @@
 
 #include <mutex>
 
+#include "../../include/lc_b200.h"
 #include "common.cuh"
 #include "lc_internal.hpp"
 
@@ -321,7 +322,9 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bf
 
 cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
                       cudaStream_t s) {
-  if (gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_tc(a, b, c, m, k, n, s);
+  std::string cfg;
+  const bool forced_simt = tune_lookup(LC_TUNE_MATMUL, m, k, n, 1 /*bf16*/, &cfg) && cfg == "simt";
+  if (!forced_simt && gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_tc(a, b, c, m, k, n, s);
   return gemm_bf16_simt(a, b, c, m, k, n, s);
 }
 

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace lcb {
 
 // Per-device state, created lazily on first use with that device current.
@@ -16,8 +18,17 @@ struct DeviceCtx {
 };
 DeviceCtx* device_ctx();
 
+// ---- auto-tune cache (tune_cache.cpp); kind: LC_TUNE_MATMUL / LC_TUNE_ATTENTION -------------
+bool tune_lookup(int kind, size_t d0, size_t d1, size_t d2, int dtype, std::string* config);
+void tune_store(int kind, size_t d0, size_t d1, size_t d2, int dtype, const std::string& config);
+
 // ---- GEMM ---------------------------------------------------------------------------------
-// Strict fp32 SIMT GEMM, C[m,n] = A[m,k] B[k,n], row-major.
+// Strict fp32 SIMT GEMM, C[m,n] = A[m,k] B[k,n], row-major.  tile < 0: default for the shape.
+cudaError_t gemm_f32_tile(const float* a, const float* b, float* c, int m, int k, int n, int tile, cudaStream_t s);
+int simt_tile_count();
+const char* simt_tile_name(int tile);
+int simt_tile_from_name(const char* name);
+// Tuned dispatch: consults the matmul auto-tune cache for (m, k, n, dtype).
 cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s);
 // bf16 in, fp32 accumulate, bf16 out.  tcgen05/TMA kernel when k%8==0 && n%8==0 and the
 // pointers are 16-byte aligned; otherwise a SIMT kernel with the same arithmetic contract.

@@ -1,0 +1,256 @@
+// Per-shape auto-tune cache, re-keyed to sm_100a kernel configurations.
+//
+// Behaviour follows the reference's Metal tune caches (src/ops/matmul_metal.mm:416-577,
+// src/attention_metal.mm:184-336): an in-memory map from shape to the chosen kernel
+// configuration, persisted as CSV with a `#lc_tune_cache,<kind>,2` header and a `#columns,...`
+// line; version 1 and 2 files load, a file with an unknown header is ignored as a whole; the file
+// path comes from CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE and is loaded on first use.
+// Keys here are (m, k, n, dtype) for matmul and (seq, head_dim, causal, dtype) for attention;
+// values are kernel configuration names ("simt128x128", "tcgen05_128x256", ...).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "lc_host.hpp"
+#include "lc_internal.hpp"
+
+namespace lcb {
+namespace {
+
+using Key = std::tuple<size_t, size_t, size_t, int>;
+
+struct Cache {
+  std::map<Key, std::string> rows;
+  bool loaded = false;  // env file consulted
+};
+
+std::mutex g_mu;
+Cache g_cache[2];
+
+const char* kind_name(int kind) { return kind == LC_TUNE_MATMUL ? "matmul" : "attention"; }
+const char* env_name(int kind) { return kind == LC_TUNE_MATMUL ? "CJ_MATMUL_TUNE_CACHE_FILE" : "CJ_ATTN_TUNE_CACHE_FILE"; }
+const char* dtype_name(int d) { return d == LC_DTYPE_BF16 ? "bf16" : d == LC_DTYPE_F64 ? "f64" : "f32"; }
+int dtype_from(const std::string& s) { return s == "bf16" ? LC_DTYPE_BF16 : s == "f64" ? LC_DTYPE_F64 : LC_DTYPE_F32; }
+const char* columns(int kind) {
+  return kind == LC_TUNE_MATMUL ? "#columns,m,k,n,dtype,config" : "#columns,seq,dim,causal,dtype,config";
+}
+
+std::vector<std::string> split(const std::string& line) {
+  std::vector<std::string> out;
+  std::stringstream ss(line);
+  std::string f;
+  while (std::getline(ss, f, ',')) out.push_back(f);
+  return out;
+}
+
+// Loads rows into `into`; returns false when the file is missing or its header is unknown.
+bool load_file(int kind, const std::string& path, std::map<Key, std::string>& into) {
+  std::ifstream in(path);
+  if (!in.is_open()) return false;
+  std::string line;
+  if (!std::getline(in, line)) return false;
+  const auto h = split(line);
+  if (h.size() != 3 || h[0] != "#lc_tune_cache" || h[1] != kind_name(kind)) return false;
+  const int version = std::atoi(h[2].c_str());
+  if (version != 1 && version != 2) return false;  // unknown format: drop every row
+  std::map<Key, std::string> rows;
+  while (std::getline(in, line)) {
+    if (line.empty() || line[0] == '#') continue;
+    const auto f = split(line);
+    // v2: d0,d1,d2,dtype,config ; v1 (no dtype column): d0,d1,d2,config with dtype f32.
+    if (version == 2 && f.size() == 5) {
+      rows[Key{std::strtoull(f[0].c_str(), nullptr, 10), std::strtoull(f[1].c_str(), nullptr, 10),
+               std::strtoull(f[2].c_str(), nullptr, 10), dtype_from(f[3])}] = f[4];
+    } else if (version == 1 && f.size() == 4) {
+      rows[Key{std::strtoull(f[0].c_str(), nullptr, 10), std::strtoull(f[1].c_str(), nullptr, 10),
+               std::strtoull(f[2].c_str(), nullptr, 10), LC_DTYPE_F32}] = f[3];
+    }
+  }
+  into.swap(rows);
+  return true;
+}
+
+bool save_file(int kind, const std::string& path, const std::map<Key, std::string>& rows) {
+  std::ofstream out(path, std::ios::out | std::ios::trunc);
+  if (!out.is_open()) return false;
+  out << "#lc_tune_cache," << kind_name(kind) << ",2\n" << columns(kind) << "\n";
+  for (const auto& kv : rows)
+    out << std::get<0>(kv.first) << "," << std::get<1>(kv.first) << "," << std::get<2>(kv.first) << ","
+        << dtype_name(std::get<3>(kv.first)) << "," << kv.second << "\n";
+  return out.good();
+}
+
+void ensure_env_loaded(int kind) {  // caller holds g_mu
+  Cache& c = g_cache[kind];
+  if (c.loaded) return;
+  c.loaded = true;
+  if (const char* p = std::getenv(env_name(kind)))
+    if (p[0]) load_file(kind, p, c.rows);
+}
+
+void persist_env(int kind) {  // caller holds g_mu
+  if (const char* p = std::getenv(env_name(kind)))
+    if (p[0]) save_file(kind, p, g_cache[kind].rows);
+}
+
+}  // namespace
+
+bool tune_lookup(int kind, size_t d0, size_t d1, size_t d2, int dtype, std::string* config) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  ensure_env_loaded(kind);
+  auto it = g_cache[kind].rows.find(Key{d0, d1, d2, dtype});
+  if (it == g_cache[kind].rows.end()) return false;
+  *config = it->second;
+  return true;
+}
+
+void tune_store(int kind, size_t d0, size_t d1, size_t d2, int dtype, const std::string& config) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  ensure_env_loaded(kind);
+  g_cache[kind].rows[Key{d0, d1, d2, dtype}] = config;
+  persist_env(kind);
+}
+
+cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
+  std::string cfg;
+  int tile = -1;
+  if (tune_lookup(LC_TUNE_MATMUL, m, k, n, LC_DTYPE_F32, &cfg)) tile = simt_tile_from_name(cfg.c_str());
+  return gemm_f32_tile(a, b, c, m, k, n, tile, s);
+}
+
+}  // namespace lcb
+
+using namespace lcb;
+
+extern "C" {
+
+lcError_t lcTuneCacheLoad(lcTuneKind kind, const char* path) {
+  if (kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) return LC_INVALID_VALUE;
+  const char* p = (path && path[0]) ? path : std::getenv(env_name(kind));
+  if (!p || !p[0]) return LC_INVALID_VALUE;
+  std::map<Key, std::string> rows;
+  if (!load_file(kind, p, rows)) return LC_NOT_SUPPORTED;  // missing file or unknown header
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_cache[kind].loaded = true;
+  g_cache[kind].rows.swap(rows);
+  return LC_SUCCESS;
+}
+
+lcError_t lcTuneCacheSave(lcTuneKind kind, const char* path) {
+  if (kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) return LC_INVALID_VALUE;
+  const char* p = (path && path[0]) ? path : std::getenv(env_name(kind));
+  if (!p || !p[0]) return LC_INVALID_VALUE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  return save_file(kind, p, g_cache[kind].rows) ? LC_SUCCESS : LC_UNKNOWN;
+}
+
+lcError_t lcTuneCacheReset(lcTuneKind kind) {
+  if (kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) return LC_INVALID_VALUE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_cache[kind].rows.clear();
+  g_cache[kind].loaded = true;  // a reset cache does not reload the env file behind the caller's back
+  return LC_SUCCESS;
+}
+
+size_t lcTuneCacheSize(lcTuneKind kind) {
+  if (kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) return 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  ensure_env_loaded(kind);
+  return g_cache[kind].rows.size();
+}
+
+lcError_t lcTuneCacheGet(lcTuneKind kind, size_t d0, size_t d1, size_t d2, lcDataType dtype, char* config,
+                         size_t cap) {
+  if ((kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) || !config || cap == 0) return LC_INVALID_VALUE;
+  std::string c;
+  if (!tune_lookup(kind, d0, d1, d2, dtype, &c)) return LC_NOT_SUPPORTED;
+  std::snprintf(config, cap, "%s", c.c_str());
+  return LC_SUCCESS;
+}
+
+lcError_t lcTuneCacheSet(lcTuneKind kind, size_t d0, size_t d1, size_t d2, lcDataType dtype, const char* config) {
+  if ((kind != LC_TUNE_MATMUL && kind != LC_TUNE_ATTENTION) || !config || !config[0] || std::strchr(config, ','))
+    return LC_INVALID_VALUE;
+  tune_store(kind, d0, d1, d2, dtype, config);
+  return LC_SUCCESS;
+}
+
+// Times every kernel configuration that can run the shape on the caller's device buffers
+// (1 warm-up + median of 5 CUDA-event samples each, like autoTuneTile in
+// src/ops/matmul_metal.mm:1643-1790), records the fastest in the cache and returns its name.
+lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
+                           lcStream_t stream, char* best, size_t cap) {
+  if (!a || !b || !out || m == 0 || k == 0 || n == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_BF16) return LC_NOT_SUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  struct Cand {
+    std::string name;
+    int tile;
+  };
+  std::vector<Cand> cands;
+  if (dtype == LC_DTYPE_F32) {
+    for (int t = 0; t < simt_tile_count(); ++t) cands.push_back({simt_tile_name(t), t});
+  } else {
+    if (gemm_bf16_tc_supported(a, b, out, (int)m, (int)k, (int)n)) cands.push_back({"tcgen05_128x256", -2});
+    cands.push_back({"simt", -1});
+  }
+  auto run = [&](const Cand& c) -> cudaError_t {
+    if (dtype == LC_DTYPE_F32)
+      return gemm_f32_tile(static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(out),
+                           (int)m, (int)k, (int)n, c.tile, s);
+    const auto* A = static_cast<const __nv_bfloat16*>(a);
+    const auto* B = static_cast<const __nv_bfloat16*>(b);
+    auto* C = static_cast<__nv_bfloat16*>(out);
+    return c.tile == -2 ? gemm_bf16_tc(A, B, C, (int)m, (int)k, (int)n, s)
+                        : gemm_bf16_simt(A, B, C, (int)m, (int)k, (int)n, s);
+  };
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return LC_DRIVER_ERROR;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return LC_DRIVER_ERROR;
+  }
+  double best_ms = 1e30;
+  std::string best_name;
+  lcError_t st = LC_SUCCESS;
+  for (const Cand& c : cands) {
+    cudaError_t e = run(c);
+    std::vector<float> ms;
+    for (int rep = 0; rep < 5 && e == cudaSuccess; ++rep) {
+      cudaEventRecord(e0, s);
+      e = run(c);
+      cudaEventRecord(e1, s);
+      if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+      float t = 0.f;
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
+      ms.push_back(t);
+    }
+    if (e != cudaSuccess) {
+      st = from_cuda(e);
+      break;
+    }
+    std::sort(ms.begin(), ms.end());
+    if (ms[ms.size() / 2] < best_ms) {
+      best_ms = ms[ms.size() / 2];
+      best_name = c.name;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (st != LC_SUCCESS) return st;
+  tune_store(LC_TUNE_MATMUL, m, k, n, dtype, best_name);
+  if (best && cap) std::snprintf(best, cap, "%s", best_name.c_str());
+  return LC_SUCCESS;
+}
+
+}  // extern "C"

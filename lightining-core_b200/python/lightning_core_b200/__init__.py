@@ -31,6 +31,7 @@ LC_SUCCESS, LC_NOT_INITIALIZED, LC_INVALID_VALUE, LC_OUT_OF_MEMORY, LC_NOT_SUPPO
 H2H, H2D, D2H, D2D = range(4)
 F32, BF16, F64 = 0, 1, 2
 LOOP_START, LOOP_RUN, LOOP_FINISH, LOOP_SYNC = range(4)
+TUNE_MATMUL, TUNE_ATTENTION = 0, 1
 
 
 class AttentionIoPolicy(C.Structure):
@@ -92,6 +93,14 @@ _SIGS = {
     "lcRuntimeTraceCount": (_sz, []),
     "lcRuntimeTraceCapacity": (_sz, []),
     "lcRuntimeTraceGet": (_i, [_sz, C.POINTER(RuntimeTraceEvent)]),
+    "lcTuneCacheLoad": (_i, [_i, C.c_char_p]),
+    "lcTuneCacheSave": (_i, [_i, C.c_char_p]),
+    "lcTuneCacheReset": (_i, [_i]),
+    "lcTuneCacheSize": (_sz, [_i]),
+    "lcTuneCacheGet": (_i, [_i, _sz, _sz, _sz, _i, C.c_char_p, _sz]),
+    "lcTuneCacheSet": (_i, [_i, _sz, _sz, _sz, _i, C.c_char_p]),
+    "lcMatMulAutotune": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, _vp, C.c_char_p, _sz]),
+    "lcConvAttentionNchwNoAlloc": (_i, [_vp] * 5 + [_sz] * 14 + [_i, _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -381,3 +390,21 @@ def layer_norm(x, eps=1e-5):
     check(lib.lcLayerNorm(dx.ptr, dy.ptr, rows, cols, eps, None), "layer_norm")
     check(lib.lcDeviceSynchronize(), "sync")
     return dy.download(x.shape, np.float32)
+
+
+# ---- auto-tune cache ------------------------------------------------------------------------
+def tune_cache_get(kind: int, d0: int, d1: int, d2: int, dtype: int = F32):
+    buf = C.create_string_buffer(64)
+    rc = lib.lcTuneCacheGet(kind, d0, d1, d2, dtype, buf, 64)
+    return buf.value.decode() if rc == LC_SUCCESS else None
+
+
+def tune_cache_set(kind: int, d0: int, d1: int, d2: int, config: str, dtype: int = F32) -> None:
+    check(lib.lcTuneCacheSet(kind, d0, d1, d2, dtype, config.encode()), "tune_cache_set")
+
+
+def matmul_autotune(a: "DeviceBuffer", b: "DeviceBuffer", out: "DeviceBuffer", m: int, k: int, n: int,
+                    dtype: int = F32) -> str:
+    buf = C.create_string_buffer(64)
+    check(lib.lcMatMulAutotune(a.ptr, b.ptr, out.ptr, m, k, n, dtype, None, buf, 64), "matmul_autotune")
+    return buf.value.decode()

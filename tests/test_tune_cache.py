@@ -1,0 +1,97 @@
+"""Auto-tune cache file format and behaviour (CPU), after the reference's
+tests/test_python_tune_cache_format_smoke.py: `#lc_tune_cache,<kind>,2` header, a `#columns,`
+line, version-1 files accepted, unknown headers rejected without touching the current rows."""
+import numpy as np
+import pytest
+
+from conftest import close_enough
+
+
+@pytest.fixture(autouse=True)
+def _clean(lc):
+    lc.lib.lcTuneCacheReset(lc.TUNE_MATMUL)
+    lc.lib.lcTuneCacheReset(lc.TUNE_ATTENTION)
+    yield
+    lc.lib.lcTuneCacheReset(lc.TUNE_MATMUL)
+    lc.lib.lcTuneCacheReset(lc.TUNE_ATTENTION)
+
+
+def test_roundtrip_v2(lc, tmp_path):
+    lc.tune_cache_set(lc.TUNE_MATMUL, 1024, 1024, 1024, "simt64x64")
+    lc.tune_cache_set(lc.TUNE_MATMUL, 8192, 8192, 8192, "tcgen05_128x256", lc.BF16)
+    lc.tune_cache_set(lc.TUNE_ATTENTION, 2048, 128, 1, "tcgen05", lc.BF16)
+    f = tmp_path / "mm.csv"
+    assert lc.lib.lcTuneCacheSave(lc.TUNE_MATMUL, str(f).encode()) == 0
+    lines = f.read_text().splitlines()
+    assert lines[0] == "#lc_tune_cache,matmul,2"
+    assert lines[1].startswith("#columns,")
+    assert "1024,1024,1024,f32,simt64x64" in lines
+    assert "8192,8192,8192,bf16,tcgen05_128x256" in lines
+    lc.lib.lcTuneCacheReset(lc.TUNE_MATMUL)
+    assert lc.lib.lcTuneCacheSize(lc.TUNE_MATMUL) == 0
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_MATMUL, str(f).encode()) == 0
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 1024, 1024, 1024) == "simt64x64"
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 8192, 8192, 8192, lc.BF16) == "tcgen05_128x256"
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 8192, 8192, 8192) is None  # dtype is part of the key
+    assert lc.tune_cache_get(lc.TUNE_ATTENTION, 2048, 128, 1, lc.BF16) == "tcgen05"
+
+
+def test_v1_rows_load_as_f32(lc, tmp_path):
+    f = tmp_path / "v1.csv"
+    f.write_text("#lc_tune_cache,matmul,1\n#columns,m,k,n,config\n256,256,256,simt128x64\n")
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_MATMUL, str(f).encode()) == 0
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 256, 256, 256) == "simt128x64"
+
+
+@pytest.mark.parametrize("header", ["#lc_tune_cache,matmul,9", "#lc_tune_cache,attention,2", "m,k,n", ""])
+def test_unknown_header_rejected(lc, tmp_path, header):
+    lc.tune_cache_set(lc.TUNE_MATMUL, 1, 2, 3, "simt64x64")
+    f = tmp_path / "bad.csv"
+    f.write_text(header + "\n4,5,6,f32,simt128x128\n")
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_MATMUL, str(f).encode()) == lc.LC_NOT_SUPPORTED
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 1, 2, 3) == "simt64x64"
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 4, 5, 6) is None
+
+
+def test_bad_arguments(lc):
+    assert lc.lib.lcTuneCacheSet(lc.TUNE_MATMUL, 1, 1, 1, 0, b"a,b") == lc.LC_INVALID_VALUE
+    assert lc.lib.lcTuneCacheSet(7, 1, 1, 1, 0, b"x") == lc.LC_INVALID_VALUE
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_MATMUL, b"/nonexistent/file.csv") == lc.LC_NOT_SUPPORTED
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cfg", ["simt128x128", "simt128x64", "simt64x64"])
+def test_every_f32_tile_config_parity(gpu, cfg):
+    from oracle import oracle as O
+
+    m, k, n = 200, 136, 72
+    rng = np.random.default_rng(1)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    gpu.tune_cache_set(gpu.TUNE_MATMUL, m, k, n, cfg)
+    close_enough(O.port().matmul(a, b), gpu.matmul2d(a, b), 1e-4, 1e-4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_autotune_records_and_is_used(gpu, dtype, tmp_path, monkeypatch):
+    from oracle import oracle as O
+
+    n = 1024
+    rng = np.random.default_rng(3)
+    a = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    b = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    dt = gpu.F32 if dtype == "f32" else gpu.BF16
+    if dt == gpu.BF16:
+        a, b = O.port().bf16_round(a / 32), O.port().bf16_round(b)
+        ha, hb = gpu.to_bf16(a), gpu.to_bf16(b)
+    else:
+        ha, hb = a, b
+    da, db = gpu.DeviceBuffer.from_array(ha), gpu.DeviceBuffer.from_array(hb)
+    dc = gpu.DeviceBuffer(n * n * (4 if dt == gpu.F32 else 2))
+    best = gpu.matmul_autotune(da, db, dc, n, n, n, dt)
+    assert gpu.tune_cache_get(gpu.TUNE_MATMUL, n, n, n, dt) == best
+    out = gpu.matmul2d(ha, hb, dtype=dt)
+    got = out if dt == gpu.F32 else gpu.from_bf16(out)
+    ref = O.port().matmul(a[:64], b, threads=8)
+    close_enough(ref, got[:64], *((1e-4, 1e-4) if dt == gpu.F32 else (2e-3, 2e-2)))
