@@ -5,8 +5,9 @@
 // then the optional postprocess out*scale + bias (ReLU) of src/attention.cpp:41-60.
 //
 // One CTA = one 128-row Q tile of one (batch, head) unit; 192 threads:
-//   warp 0      TMA: Q once, then K_j and V_j tiles (128 keys) into two 2-stage rings (K freed
-//               once S_j is done, V once PV_j is done, so loads run ahead of the MMAs); 3-D tensor
+//   warp 0      TMA: Q once, then K_j tiles (64 keys) into a 2-stage ring freed as soon as S_j
+//               is done; warp 6 loads V_j into its own buffer freed by PV_j (a separate thread,
+//               so a late V slot never holds back K); L2 prefetch of upcoming tiles; 3-D tensor
 //               maps [units, S, D] so rows past S read as zero; 128-byte swizzle.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1}
 //               overlaps the softmax of S_j), then O += P_j V_j once P_j is in shared memory.
@@ -41,10 +42,10 @@ constexpr int TILE = 128;               // query rows per CTA (= TMEM lanes)
 constexpr int TK = 64;                  // keys per KV tile
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
 constexpr int KCHUNK_BYTES = TK * 128;  // one [64 rows x 64 bf16] swizzled box = 8 KB
-constexpr int K_STAGES = 1;   // K_{j+1} refills as soon as S_j is done: ~a softmax of slack
-constexpr int V_STAGES = 2;   // V_{j+1} refills once PV_{j-1} is done
+constexpr int K_STAGES = 2;  // K_{j+2} loads as soon as S_j is done
+constexpr int V_STAGES = 1;  // V_{j+1} loads once PV_j is done (a separate producer thread)
 constexpr int P_BUFS = 2;     // P_j goes to buffer j%2, so softmax j never waits for PV_{j-1}
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 224;  // 7 warps: K/Q loader, MMA, 4 softmax, V loader
 constexpr uint32_t TMEM_COLS = 256;  // S buffers at 0 and 64, O at 128: two CTAs fit one SM
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float RESCALE_THRESHOLD = 8.0f;
@@ -202,22 +203,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   const uint32_t tmem = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
 
+  // Bounded drain of copies already issued, so the CTA never exits with TMA writes in flight.
+  auto drain = [](uint64_t* bar, uint32_t ph) {
+    const uint64_t t1 = globaltimer_ns();
+    while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t1 < 100000000ull) {
+    }
+  };
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer: Q and K
     if (lane == 0) {
-      int issued = 0;
       bool ok = true;
       mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
       load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
       int k_issued = 0;
       for (int j = 0; j < n_kv; ++j) {
-        const int ks = j % K_STAGES, vs = j % V_STAGES;
-        if (j + 1 < n_kv) {  // warm L2 for the next K/V tiles while this one waits for its slot
-          for (int c = 0; c < NCH; ++c) {
-            tma_prefetch_l2_3d(&map_k, c * 64, (j + 1) * TK, unit);
-            tma_prefetch_l2_3d(&map_v, c * 64, (j + 1) * TK, unit);
-          }
-        }
+        const int ks = j % K_STAGES;
+        if (j + K_STAGES < n_kv)  // warm L2 for the K tile that will take this slot next
+          for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + K_STAGES) * TK, unit);
         if (!mbar_wait_bounded(&st->k_empty[ks], ((j / K_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
                                kErrAttnLoadWait)) {
           ok = false;
@@ -226,6 +228,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         mbar_arrive_expect_tx(&st->k_full[ks], LY::KV_BYTES);
         load_rows(sK + ks * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[ks]);
         ++k_issued;
+      }
+      if (!ok) {
+        drain(&st->q_full, 0);
+        for (int j = k_issued > K_STAGES ? k_issued - K_STAGES : 0; j < k_issued; ++j)
+          drain(&st->k_full[j % K_STAGES], (j / K_STAGES) & 1);
+      }
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ TMA producer: V
+    // A separate thread, so a V slot that frees late never holds back the next K load.
+    if (lane == 0) {
+      bool ok = true;
+      int v_issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int vs = j % V_STAGES;
+        if (j + V_STAGES < n_kv)
+          for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
         if (!mbar_wait_bounded(&st->v_empty[vs], ((j / V_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
                                kErrAttnLoadWait)) {
           ok = false;
@@ -233,23 +252,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
         mbar_arrive_expect_tx(&st->v_full[vs], LY::KV_BYTES);
         load_rows(sV + vs * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[vs]);
-        ++issued;
+        ++v_issued;
       }
-      if (!ok) {
-        // Let already-issued copies land before the CTA exits (bounded).
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&st->q_full, 0) && globaltimer_ns() - t0 < 100000000ull) {
-        }
-        auto drain = [](uint64_t* bar, uint32_t ph) {
-          const uint64_t t1 = globaltimer_ns();
-          while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t1 < 100000000ull) {
-          }
-        };
-        for (int j = k_issued > K_STAGES ? k_issued - K_STAGES : 0; j < k_issued; ++j)
-          drain(&st->k_full[j % K_STAGES], (j / K_STAGES) & 1);
-        for (int j = issued > V_STAGES ? issued - V_STAGES : 0; j < issued; ++j)
+      if (!ok)
+        for (int j = v_issued > V_STAGES ? v_issued - V_STAGES : 0; j < v_issued; ++j)
           drain(&st->v_full[j % V_STAGES], (j / V_STAGES) & 1);
-      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -312,7 +319,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
       }
     }
-  } else {
+  } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // row within the Q tile == TMEM lane
