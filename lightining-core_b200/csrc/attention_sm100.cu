@@ -54,8 +54,6 @@ struct AttnTail {
   uint64_t q_full;
   uint64_t k_full[K_STAGES];
   uint64_t v_full[V_STAGES];
-  uint64_t k_empty[K_STAGES];  // K_j consumed by S_j: refilled early, independent of PV
-  uint64_t v_empty[V_STAGES];  // V_j consumed by PV_j
   uint64_t s_full[2];
   uint64_t p_full;
   uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
@@ -173,14 +171,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(&st->q_full, 1);
-    for (int s = 0; s < K_STAGES; ++s) {
-      mbar_init(&st->k_full[s], 1);
-      mbar_init(&st->k_empty[s], 1);
-    }
-    for (int s = 0; s < V_STAGES; ++s) {
-      mbar_init(&st->v_full[s], 1);
-      mbar_init(&st->v_empty[s], 1);
-    }
+    for (int s = 0; s < K_STAGES; ++s) mbar_init(&st->k_full[s], 1);
+    for (int s = 0; s < V_STAGES; ++s) mbar_init(&st->v_full[s], 1);
     mbar_init(&st->s_full[0], 1);
     mbar_init(&st->s_full[1], 1);
     mbar_init(&st->p_full, 4);
@@ -220,8 +212,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const int ks = j % K_STAGES;
         if (j + K_STAGES < n_kv)  // warm L2 for the K tile that will take this slot next
           for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + K_STAGES) * TK, unit);
-        if (!mbar_wait_bounded(&st->k_empty[ks], ((j / K_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
-                               kErrAttnLoadWait)) {
+        // Slot ks last held K_{j-2}: S_{j-2} must have finished reading it.  Every MMA group has
+        // exactly one commit (S_j -> s_full[j&1]), and this thread observes S_0, S_1, ... in
+        // order, so each parity wait is unambiguous.
+        if (j >= K_STAGES && !mbar_wait_bounded(&st->s_full[(j - K_STAGES) & 1], ((j - K_STAGES) >> 1) & 1,
+                                                abort_flag, p.err_word, kErrAttnLoadWait)) {
           ok = false;
           break;
         }
@@ -245,8 +240,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const int vs = j % V_STAGES;
         if (j + V_STAGES < n_kv)
           for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
-        if (!mbar_wait_bounded(&st->v_empty[vs], ((j / V_STAGES) & 1) ^ 1u, abort_flag, p.err_word,
-                               kErrAttnLoadWait)) {
+        // The single V buffer last held V_{j-1}: PV_{j-1} (one commit: o_done[(j-1)%2]) must be done.
+        if (j >= V_STAGES && !mbar_wait_bounded(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag,
+                                                p.err_word, kErrAttnLoadWait)) {
           ok = false;
           break;
         }
@@ -282,8 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                       IDESC_S, kk > 0 ? 1u : 0u);
         }
         issued = true;
-        umma_commit(&st->s_full[j & 1]);
-        umma_commit(&st->k_empty[s]);
+        umma_commit(&st->s_full[j & 1]);  // the only commit of this MMA group
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -309,8 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, KCHUNK_BYTES, 1024);
           umma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&st->v_empty[s]);
-        umma_commit(&st->o_done[j % P_BUFS]);
+        umma_commit(&st->o_done[j % P_BUFS]);  // the only commit of this MMA group
       }
       if (!ok && issued) {
         umma_commit(&st->drain);

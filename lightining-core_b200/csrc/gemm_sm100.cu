@@ -218,7 +218,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tbase + c0, r);
-        tmem_wait_ld();
         const int col = nb * BN + c0;
         if (row < M && col < N) {
           if (vec_ok && col + 32 <= N) {
