@@ -208,3 +208,21 @@ def test_device_runtime(gpu):
     assert L.lcDeviceSynchronize() == 0
     code = C.c_uint(123)
     assert L.lcGetDeviceErrorWord(C.byref(code)) == 0 and code.value == 0
+
+
+@pytest.mark.parametrize("units,s,d,causal", [(128, 2048, 128, 1), (40, 2048, 128, 0), (300, 256, 128, 1),
+                                              (7, 3333, 128, 1), (128, 2048, 64, 1), (16, 4096, 128, 1)])
+def test_attention_bf16_stress_vs_torch_fp32(gpu, units, s, d, causal):
+    """Many-CTA shapes (every TMEM/P-buffer hand-off exercised thousands of times) against a float32
+    reference computed on the device from the same bf16 inputs; all heads, all rows."""
+    import torch
+
+    torch.manual_seed(units + s)
+    q, k, v = (torch.randn((units, s, d), device="cuda").to(torch.bfloat16) for _ in range(3))
+    o = torch.zeros_like(q)
+    gpu.check(gpu.lib.lcAttentionForward(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()),
+                                         C.c_void_p(o.data_ptr()), units, s, d, causal, gpu.BF16, None, None))
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=bool(causal))
+    err = (o.float() - ref).abs()
+    assert bool((err <= 2e-2 + 2e-2 * ref.abs()).all()), float(err.max())
