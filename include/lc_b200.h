@@ -251,6 +251,37 @@ lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataT
  * (the reference's LN formula, README.md:2267-2270).  Device pointers, fp32. */
 lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, float eps, lcStream_t stream);
 
+/* ---- device-resident sessions ----------------------------------------------------------------
+ * AttentionSession (include/lightning_core/core/attention.hpp:86-129, src/attention.cpp:247-343) and
+ * MatMulMetalResidentSession (include/lightning_core/core/ops.hpp:1339-1379): a handle bound to one
+ * shape owning device buffers that persist between calls.  Policy flags: upload_* set -> copy that
+ * HOST pointer into the session buffer; clear -> reuse the buffer as it is (pointer may be NULL);
+ * download_out set -> copy the result to HOST `out`; synchronize -> wait on `stream`.  Buffers can be
+ * filled or read directly through lcAttentionSessionBuffer / lcMatMulSessionBuffer (device
+ * pointers; which = 0 q|a, 1 k|b, 2 v (attention) / out (matmul), 3 out (attention)).  Calls on one
+ * session from several threads serialise on a per-session lock. */
+typedef struct lcAttentionSession* lcAttentionSession_t;
+typedef struct lcMatMulSession* lcMatMulSession_t;
+lcError_t lcAttentionSessionCreate(lcAttentionSession_t* out, size_t units, size_t seq, size_t head_dim, int causal,
+                                   lcDataType dtype);
+lcError_t lcAttentionSessionDestroy(lcAttentionSession_t s);
+/* Default policy for calls that pass NULL; starts as the reference session default
+ * (everything uploaded/downloaded, synchronize = 0). */
+lcError_t lcAttentionSessionSetDefaultPolicy(lcAttentionSession_t s, const lcAttentionIoPolicy* policy);
+lcError_t lcAttentionSessionBuffer(lcAttentionSession_t s, int which, void** dev_ptr);
+lcError_t lcAttentionSessionForward(lcAttentionSession_t s, const void* q, const void* k, const void* v, void* out,
+                                    const lcAttentionIoPolicy* policy, lcStream_t stream);
+lcError_t lcMatMulSessionCreate(lcMatMulSession_t* out, size_t m, size_t k, size_t n, lcDataType dtype);
+lcError_t lcMatMulSessionDestroy(lcMatMulSession_t s);
+lcError_t lcMatMulSessionBuffer(lcMatMulSession_t s, int which, void** dev_ptr);
+/* One call; drive a resident loop with lcMatMulPolicyForStage(START / RUN / FINISH / SYNC). */
+lcError_t lcMatMulSessionRun(lcMatMulSession_t s, const void* a, const void* b, void* out,
+                             const lcMatMulIoPolicy* policy, lcStream_t stream);
+/* runBatchSync / runBatchSyncNoDownload (ops.hpp:251-352): upload a / b when non-NULL, launch
+ * `repeat` times on the resident buffers, synchronize once, download when out != NULL. */
+lcError_t lcMatMulSessionRunBatch(lcMatMulSession_t s, const void* a, const void* b, void* out, size_t repeat,
+                                  lcStream_t stream);
+
 /* ---- per-shape auto-tune cache (src/ops/matmul_metal.mm:416-577, src/attention_metal.mm:184-336) */
 /* CSV `#lc_tune_cache,<matmul|attention>,2` + `#columns,...`; keys (m,k,n,dtype) for matmul and
  * (seq,head_dim,causal,dtype) for attention; values are sm_100a kernel configuration names

@@ -101,6 +101,16 @@ _SIGS = {
     "lcTuneCacheSet": (_i, [_i, _sz, _sz, _sz, _i, C.c_char_p]),
     "lcMatMulAutotune": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, _vp, C.c_char_p, _sz]),
     "lcConvAttentionNchwNoAlloc": (_i, [_vp] * 5 + [_sz] * 14 + [_i, _vp]),
+    "lcAttentionSessionCreate": (_i, [C.POINTER(_vp), _sz, _sz, _sz, _i, _i]),
+    "lcAttentionSessionDestroy": (_i, [_vp]),
+    "lcAttentionSessionSetDefaultPolicy": (_i, [_vp, C.POINTER(AttentionIoPolicy)]),
+    "lcAttentionSessionBuffer": (_i, [_vp, _i, C.POINTER(_vp)]),
+    "lcAttentionSessionForward": (_i, [_vp, _vp, _vp, _vp, _vp, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcMatMulSessionCreate": (_i, [C.POINTER(_vp), _sz, _sz, _sz, _i]),
+    "lcMatMulSessionDestroy": (_i, [_vp]),
+    "lcMatMulSessionBuffer": (_i, [_vp, _i, C.POINTER(_vp)]),
+    "lcMatMulSessionRun": (_i, [_vp, _vp, _vp, _vp, C.POINTER(MatMulIoPolicy), _vp]),
+    "lcMatMulSessionRunBatch": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -408,3 +418,101 @@ def matmul_autotune(a: "DeviceBuffer", b: "DeviceBuffer", out: "DeviceBuffer", m
     buf = C.create_string_buffer(64)
     check(lib.lcMatMulAutotune(a.ptr, b.ptr, out.ptr, m, k, n, dtype, None, buf, 64), "matmul_autotune")
     return buf.value.decode()
+
+
+# ---- sessions (AttentionSession / MatMulMetalResidentSession of the reference) ---------------
+class AttentionSession:
+    """attention.hpp:86-129: a shape-bound handle with device-resident q/k/v/out buffers."""
+
+    def __init__(self, seq_len: int, head_dim: int, causal: bool = False, units: int = 1, dtype: int = F32):
+        self.shape = (units, seq_len, head_dim) if units > 1 else (seq_len, head_dim)
+        self.np_dtype = np.float32 if dtype == F32 else np.uint16
+        self.h = C.c_void_p()
+        check(lib.lcAttentionSessionCreate(C.byref(self.h), units, seq_len, head_dim, int(causal), dtype),
+              "AttentionSession")
+
+    def set_default_policy(self, policy: AttentionIoPolicy) -> None:
+        check(lib.lcAttentionSessionSetDefaultPolicy(self.h, C.byref(policy)))
+
+    def forward_with_policy(self, q, k, v, out, policy: AttentionIoPolicy):
+        arrs = [None if x is None else np.ascontiguousarray(x, dtype=self.np_dtype) for x in (q, k, v)]
+        check(lib.lcAttentionSessionForward(self.h, *[_vp(x) for x in arrs], _vp(out), C.byref(policy), None),
+              "AttentionSession.forward")
+        return out
+
+    def forward(self, q, k, v):
+        out = np.empty(self.shape, self.np_dtype)
+        check(lib.lcAttentionSessionForward(self.h, *[_vp(np.ascontiguousarray(x, dtype=self.np_dtype))
+                                                      for x in (q, k, v)], _vp(out), None, None),
+              "AttentionSession.forward")
+        lib.lcDeviceSynchronize()
+        return out
+
+    def buffer(self, which: int) -> int:
+        p = C.c_void_p()
+        check(lib.lcAttentionSessionBuffer(self.h, which, C.byref(p)))
+        return p.value
+
+    def close(self) -> None:
+        if self.h and self.h.value:
+            lib.lcAttentionSessionDestroy(self.h)
+        self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class MatMulResidentSession:
+    """ops.hpp:1339-1379 (MatMulMetalResidentSession): start / run / finish / sync / run_batch_sync."""
+
+    def __init__(self, m: int, k: int, n: int, dtype: int = F32):
+        self.m, self.k, self.n = m, k, n
+        self.np_dtype = np.float32 if dtype == F32 else np.uint16
+        self.h = C.c_void_p()
+        check(lib.lcMatMulSessionCreate(C.byref(self.h), m, k, n, dtype), "MatMulResidentSession")
+
+    def _stage(self, stage, a, b, out):
+        pol = matmul_policy_for_stage(stage)
+        pa = None if a is None else np.ascontiguousarray(a, dtype=self.np_dtype)
+        pb = None if b is None else np.ascontiguousarray(b, dtype=self.np_dtype)
+        check(lib.lcMatMulSessionRun(self.h, _vp(pa), _vp(pb), _vp(out), C.byref(pol), None), "matmul session")
+        return out
+
+    def start(self, a, b):
+        return self._stage(LOOP_START, a, b, None)
+
+    def run(self):
+        return self._stage(LOOP_RUN, None, None, None)
+
+    def finish(self):
+        out = np.empty((self.m, self.n), self.np_dtype)
+        return self._stage(LOOP_FINISH, None, None, out)
+
+    def sync(self):
+        return self._stage(LOOP_SYNC, None, None, None)
+
+    def run_batch_sync(self, a, b, repeat: int, download: bool = True):
+        out = np.empty((self.m, self.n), self.np_dtype) if download else None
+        pa = None if a is None else np.ascontiguousarray(a, dtype=self.np_dtype)
+        pb = None if b is None else np.ascontiguousarray(b, dtype=self.np_dtype)
+        check(lib.lcMatMulSessionRunBatch(self.h, _vp(pa), _vp(pb), _vp(out), repeat, None), "run_batch_sync")
+        return out
+
+    def buffer(self, which: int) -> int:
+        p = C.c_void_p()
+        check(lib.lcMatMulSessionBuffer(self.h, which, C.byref(p)))
+        return p.value
+
+    def close(self) -> None:
+        if self.h and self.h.value:
+            lib.lcMatMulSessionDestroy(self.h)
+        self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
