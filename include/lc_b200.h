@@ -204,6 +204,16 @@ lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* 
 lcError_t lcMatMul(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
                    const lcMatMulIoPolicy* policy, lcStream_t stream);
 
+/* attentionTrainStepWithPolicy (src/attention.cpp:216-242; CPU src/attention_cpu.cpp:114-163):
+ * forward (written to `out`), MSE loss against `target`, dV = P^T dO with dO = 2(out - target)/(seq*d),
+ * v -= learning_rate * dV in place.  fp32, head_dim <= 128, `units` heads [units, seq, head_dim].
+ * learning_rate <= 0 -> LC_INVALID_VALUE.  loss_out (host, may be NULL) receives one loss per unit
+ * (mean squared error, as the reference).  Policy: upload_q/k/v/target mark host inputs;
+ * download_out / download_v copy `out` / the updated `v` back to host memory. */
+lcError_t lcAttentionTrainStep(const float* q, const float* k, float* v, const float* target, float* out,
+                               float learning_rate, size_t units, size_t seq, size_t head_dim, int causal,
+                               float* loss_out, const lcAttentionIoPolicy* policy, lcStream_t stream);
+
 /* NCHW x OIHW (+bias, may be NULL) -> NCHW, optional ReLU; replaces ops::conv2dNchw<float>
  * (include/lightning_core/core/ops.hpp:855-1212).  fp32 strict implicit GEMM. */
 lcError_t lcConv2dNchw(const float* x, const float* w, const float* bias, float* out, size_t batch,
@@ -271,6 +281,13 @@ lcError_t lcAttentionSessionSetDefaultPolicy(lcAttentionSession_t s, const lcAtt
 lcError_t lcAttentionSessionBuffer(lcAttentionSession_t s, int which, void** dev_ptr);
 lcError_t lcAttentionSessionForward(lcAttentionSession_t s, const void* q, const void* k, const void* v, void* out,
                                     const lcAttentionIoPolicy* policy, lcStream_t stream);
+/* AttentionSession::trainStepWithPolicy (src/attention.cpp:301-343): one train step on the
+ * session's resident q/k/v (v updated in place, so repeated steps train it); `target` follows
+ * upload_target.  With loss_out, the loss is computed every loss_every-th step (0 -> the
+ * reference's shape-aware default) and the last sampled loss is returned in between. */
+lcError_t lcAttentionSessionTrainStep(lcAttentionSession_t s, const float* q, const float* k, float* v,
+                                      const float* target, float* out, float learning_rate, float* loss_out,
+                                      const lcAttentionIoPolicy* policy, lcStream_t stream);
 lcError_t lcMatMulSessionCreate(lcMatMulSession_t* out, size_t m, size_t k, size_t n, lcDataType dtype);
 lcError_t lcMatMulSessionDestroy(lcMatMulSession_t s);
 lcError_t lcMatMulSessionBuffer(lcMatMulSession_t s, int which, void** dev_ptr);

@@ -162,6 +162,15 @@ __global__ void __launch_bounds__(NT) attn_simt_kernel(AttnArgs a) {
     }
   }
 
+  // Row log-sum-exp (natural log, scaled-score units) for the train step's dV recomputation.
+  if (a.lse != nullptr && cg == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gi = q0 + rg * 4 + i;
+      if (gi < S) a.lse[static_cast<long long>(unit) * S + gi] = m[i] + logf(l[i]);
+    }
+  }
+
   // Normalise, postprocess.
   const bool post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
 #pragma unroll
@@ -242,7 +251,174 @@ cudaError_t dispatch(const AttnArgs& a, cudaStream_t s) {
   return cudaErrorNotSupported;
 }
 
+// ---- train step (src/attention_cpu.cpp:114-163) ------------------------------------------------
+
+// dO = 2 (O - T) / (seq*d); sse[u] += sum (O - T)^2 over unit u (double accumulation).
+__global__ void train_grad_out_kernel(const float* __restrict__ out, const float* __restrict__ target,
+                                      float* __restrict__ dout, double* __restrict__ sse, long long per_unit) {
+  const int unit = blockIdx.y;
+  const float norm = 1.0f / static_cast<float>(per_unit);
+  const long long base = static_cast<long long>(unit) * per_unit;
+  double acc = 0.0;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < per_unit;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float diff = out[base + i] - target[base + i];
+    acc += static_cast<double>(diff) * diff;
+    dout[base + i] = 2.0f * diff * norm;
+  }
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  __shared__ double part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += part[w];
+    atomicAdd(sse + unit, t);
+  }
+}
+
+// dV for a tile of 64 keys, recomputing P^T = exp(K Q^T * scale - lse) tile by tile (no S x S
+// buffer), accumulating dV[j] = sum_i P[i][j] dO[i] over query rows i in increasing order (the
+// reference's loop order), then v[j] -= lr * dV[j] in place (dV never reads v).
+// Same thread layout as attn_simt_kernel: thread t owns keys (t>>4)*4 .. +3 of the tile.
+template <int DP>
+__global__ void __launch_bounds__(NT) attn_dv_kernel(const float* __restrict__ q, const float* __restrict__ k,
+                                                     float* __restrict__ v, const float* __restrict__ dout,
+                                                     const float* __restrict__ lse, int S, int D, int causal,
+                                                     float scale, float lr) {
+  extern __shared__ __align__(16) float smem[];
+  float* Kt = smem;              // [DP][TK]  keys of this block (the "rows" here)
+  float* Qt = Kt + DP * TK;      // [DP][TQ]  query rows of the current tile
+  float* Gs = Qt + DP * TQ;      // [TQ][DP]  dO rows of the current tile
+  float* Pt = Gs + TQ * DP;      // [TQ][TK]  P^T tile: Pt[i][j]
+  float* Ls = Pt + TQ * TK;      // [TQ]      lse of the current query rows
+  const int tid = threadIdx.x;
+  const int rg = tid >> 4, cg = tid & 15;
+  const int unit = blockIdx.y;
+  const int k0 = blockIdx.x * TK;
+  const long long ub = static_cast<long long>(unit) * S * D;
+  for (int idx = tid; idx < TK * DP; idx += NT) {
+    const int j = idx % TK, c = idx / TK;
+    const int gj = k0 + j;
+    Kt[c * TK + j] = (gj < S && c < D) ? k[ub + static_cast<long long>(gj) * D + c] : 0.0f;
+  }
+  constexpr int DC = DP / 16;
+  float dv[4][DC];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < DC; ++j) dv[i][j] = 0.0f;
+
+  // Causal: query rows i < k0 see none of these keys.
+  const int qt0 = causal ? k0 / TQ : 0;
+  const int nqt = (S + TQ - 1) / TQ;
+  for (int t = qt0; t < nqt; ++t) {
+    const int i0 = t * TQ;
+    __syncthreads();
+    for (int idx = tid; idx < TQ * DP; idx += NT) {
+      const int r = idx % TQ, c = idx / TQ;
+      const int gi = i0 + r;
+      Qt[c * TQ + r] = (gi < S && c < D) ? q[ub + static_cast<long long>(gi) * D + c] : 0.0f;
+    }
+    for (int idx = tid; idx < TQ * DP; idx += NT) {
+      const int c = idx % DP, r = idx / DP;
+      const int gi = i0 + r;
+      Gs[r * DP + c] = (gi < S && c < D) ? dout[ub + static_cast<long long>(gi) * D + c] : 0.0f;
+    }
+    for (int r = tid; r < TQ; r += NT) Ls[r] = (i0 + r < S) ? lse[static_cast<long long>(unit) * S + i0 + r] : 0.0f;
+    __syncthreads();
+    // S^T[j][i] for this thread's 4 keys x 4 query rows (cols cg*4..).
+    float st[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) st[a][b] = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < DP; ++c) {
+      const float4 ka = *reinterpret_cast<const float4*>(Kt + c * TK + rg * 4);
+      const float4 qb = *reinterpret_cast<const float4*>(Qt + c * TQ + cg * 4);
+      const float kv[4] = {ka.x, ka.y, ka.z, ka.w};
+      const float qv[4] = {qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) st[a][b] = fmaf(kv[a], qv[b], st[a][b]);
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int gj = k0 + rg * 4 + a;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int li = cg * 4 + b, gi = i0 + li;
+        float pv = expf(st[a][b] * scale - Ls[li]);
+        if (gi >= S || gj >= S || (causal && gj > gi)) pv = 0.0f;
+        Pt[li * TK + rg * 4 + a] = pv;
+      }
+    }
+    __syncthreads();
+    const int imax = min(TQ, S - i0);
+#pragma unroll 4
+    for (int i = 0; i < imax; ++i) {
+      const float4 pa = *reinterpret_cast<const float4*>(Pt + i * TK + rg * 4);
+      const float pv[4] = {pa.x, pa.y, pa.z, pa.w};
+#pragma unroll
+      for (int g = 0; g < DP / 64; ++g) {
+        const float4 gb = *reinterpret_cast<const float4*>(Gs + i * DP + (g * 16 + cg) * 4);
+        const float gv[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dv[a][g * 4 + e] = fmaf(pv[a], gv[e], dv[a][g * 4 + e]);
+      }
+    }
+  }
+  // SGD on V (src/attention_cpu.cpp:157-159).
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int gj = k0 + rg * 4 + a;
+    if (gj >= S) continue;
+#pragma unroll
+    for (int g = 0; g < DP / 64; ++g)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int c = (g * 16 + cg) * 4 + e;
+        if (c < D) v[ub + static_cast<long long>(gj) * D + c] -= lr * dv[a][g * 4 + e];
+      }
+  }
+}
+
+template <int DP>
+cudaError_t launch_dv(const float* q, const float* k, float* v, const float* dout, const float* lse, int units, int S,
+                      int D, int causal, float scale, float lr, cudaStream_t s) {
+  const size_t smem = sizeof(float) * (DP * TK + DP * TQ + TQ * DP + TQ * TK + TQ);
+  cudaError_t e = cudaFuncSetAttribute(attn_dv_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  dim3 grid((S + TK - 1) / TK, units);
+  if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
+  attn_dv_kernel<DP><<<grid, NT, smem, s>>>(q, k, v, dout, lse, S, D, causal, scale, lr);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t attention_train_grad_out(const float* out, const float* target, float* dout, double* sse, int units,
+                                     long long per_unit, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(sse, 0, sizeof(double) * units, s);
+  if (e != cudaSuccess) return e;
+  long long blocks = (per_unit + 255) / 256;
+  if (blocks > 64) blocks = 64;
+  if (units > 65535) return cudaErrorInvalidConfiguration;
+  train_grad_out_kernel<<<dim3(static_cast<unsigned>(blocks), units), 256, 0, s>>>(out, target, dout, sse, per_unit);
+  return cudaGetLastError();
+}
+
+cudaError_t attention_train_dv_update(const float* q, const float* k, float* v, const float* dout, const float* lse,
+                                      int units, int seq, int d, int causal, float scale, float lr, cudaStream_t s) {
+  if (d <= 64) return launch_dv<64>(q, k, v, dout, lse, units, seq, d, causal, scale, lr, s);
+  if (d <= 128) return launch_dv<128>(q, k, v, dout, lse, units, seq, d, causal, scale, lr, s);
+  return cudaErrorNotSupported;
+}
 
 cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s) { return dispatch<float>(a, s); }
 cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s) { return dispatch<__nv_bfloat16>(a, s); }

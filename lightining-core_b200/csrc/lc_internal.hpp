@@ -62,8 +62,15 @@ struct AttnArgs {
   int post_relu;         // out = relu?(out*post_scale + post_bias)
   const float* proj_w;   // optional [d, proj_cols] fused projection (fp32 path only)
   int proj_cols;
+  float* lse;            // optional [units, seq] log-sum-exp of the scaled scores (fp32 path only)
 };
 cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s);
+// Train step pieces (fp32): dO = 2(O - T)/(seq*d) and per-unit sum of squared errors (double);
+// then dV = P^T dO recomputed from Q, K and the forward's LSE, applied as v -= lr * dV in place.
+cudaError_t attention_train_grad_out(const float* out, const float* target, float* dout, double* sse, int units,
+                                     long long per_unit, cudaStream_t s);
+cudaError_t attention_train_dv_update(const float* q, const float* k, float* v, const float* dout, const float* lse,
+                                      int units, int seq, int d, int causal, float scale, float lr, cudaStream_t s);
 cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s);
 bool attention_bf16_tc_supported(const AttnArgs& a);

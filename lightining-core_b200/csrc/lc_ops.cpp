@@ -359,3 +359,73 @@ lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, floa
 }
 
 }  // extern "C"
+
+// attentionTrainStepWithPolicy (src/attention.cpp:216-242) + attentionTrainStepCpu
+// (src/attention_cpu.cpp:114-163): forward, MSE against target, dV = P^T dO, v -= lr * dV.
+// Batched over `units` heads; loss_out (optional, host) receives one loss per unit.
+extern "C" lcError_t lcAttentionTrainStep(const float* q, const float* k, float* v, const float* target, float* out,
+                                          float learning_rate, size_t units, size_t seq, size_t head_dim, int causal,
+                                          float* loss_out, const lcAttentionIoPolicy* policy, lcStream_t stream) {
+  if (!q || !k || !v || !target || !out || units == 0 || seq == 0 || head_dim == 0 || !(learning_rate > 0.0f))
+    return LC_INVALID_VALUE;
+  if (head_dim > 128 || seq > (size_t)INT_MAX || units > 65535) return LC_NOT_SUPPORTED;
+  lcAttentionIoPolicy pol;
+  if (policy) {
+    pol = *policy;
+  } else {
+    lcAttentionIoPolicyDefault(&pol);
+    pol.upload_q = pol.upload_k = pol.upload_v = pol.upload_target = 0;
+    pol.download_out = pol.download_v = pol.synchronize = 0;
+  }
+  Io io(static_cast<cudaStream_t>(stream));
+  cudaStream_t s = io.stream();
+  const size_t n = units * seq * head_dim, bytes = n * 4;
+  const void *dq, *dk, *dt;
+  void *dvv, *dout, *lse, *grad, *sse;
+  LC_TRY(io.in(q, bytes, pol.upload_q, &dq));
+  LC_TRY(io.in(k, bytes, pol.upload_k, &dk));
+  LC_TRY(io.in(target, bytes, pol.upload_target, &dt));
+  {
+    const void* vin;
+    LC_TRY(io.in(v, bytes, pol.upload_v, &vin));  // staged copy when v is host memory
+    dvv = const_cast<void*>(vin);
+  }
+  LC_TRY(io.out(out, bytes, pol.download_out, &dout));
+  LC_TRY(io.scratch(units * seq * 4, &lse));
+  LC_TRY(io.scratch(bytes, &grad));
+  LC_TRY(io.scratch(units * sizeof(double), &sse));
+  trace_op(kOpAttention, units * seq * seq * head_dim);
+  AttnArgs a{};
+  a.q = dq;
+  a.k = dk;
+  a.v = dvv;
+  a.out = dout;
+  a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = a.out_unit_stride = static_cast<long long>(seq * head_dim);
+  a.units = static_cast<int>(units);
+  a.seq = static_cast<int>(seq);
+  a.d = static_cast<int>(head_dim);
+  a.causal = causal ? 1 : 0;
+  a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+  a.post_scale = 1.0f;
+  a.lse = static_cast<float*>(lse);
+  LC_TRY(attention_f32(a, s));
+  LC_TRY(attention_train_grad_out(static_cast<const float*>(dout), static_cast<const float*>(dt),
+                                  static_cast<float*>(grad), static_cast<double*>(sse), (int)units,
+                                  static_cast<long long>(seq * head_dim), s));
+  LC_TRY(attention_train_dv_update(static_cast<const float*>(dq), static_cast<const float*>(dk),
+                                   static_cast<float*>(dvv), static_cast<const float*>(grad),
+                                   static_cast<const float*>(lse), (int)units, (int)seq, (int)head_dim, a.causal,
+                                   a.scale, learning_rate, s));
+  if (pol.download_v) LC_TRY(cudaMemcpyAsync(v, dvv, bytes, cudaMemcpyDeviceToHost, s));
+  if (pol.download_out) LC_TRY(cudaMemcpyAsync(out, dout, bytes, cudaMemcpyDeviceToHost, s));
+  if (loss_out) {
+    std::vector<double> h(units);
+    LC_TRY(cudaMemcpyAsync(h.data(), sse, units * sizeof(double), cudaMemcpyDeviceToHost, s));
+    LC_TRY(cudaStreamSynchronize(s));
+    const float norm = 1.0f / static_cast<float>(seq * head_dim);
+    for (size_t u = 0; u < units; ++u) loss_out[u] = static_cast<float>(h[u]) * norm;
+  }
+  const bool synced = pol.synchronize || pol.download_out || pol.download_v || loss_out;
+  if (synced) LC_TRY(cudaStreamSynchronize(s));
+  return check_error_word(synced);
+}

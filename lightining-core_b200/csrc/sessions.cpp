@@ -13,6 +13,7 @@
 
 #include <mutex>
 #include <new>
+#include <vector>
 
 #include "lc_host.hpp"
 #include "lc_internal.hpp"
@@ -59,7 +60,11 @@ struct lcAttentionSession {
   int causal;
   lcDataType dtype;
   int device;
-  Buf b[4];  // q, k, v, out
+  Buf b[4];       // q, k, v, out
+  Buf target;     // allocated by the first train step
+  size_t train_steps = 0;
+  std::vector<float> last_loss;
+  bool has_last_loss = false;
   lcAttentionIoPolicy def;
   std::mutex mu;
 };
@@ -101,6 +106,7 @@ lcError_t lcAttentionSessionCreate(lcAttentionSession_t* out, size_t units, size
 lcError_t lcAttentionSessionDestroy(lcAttentionSession_t s) {
   if (!s) return LC_INVALID_VALUE;
   for (auto& x : s->b) cudaFree(x.p);
+  if (s->target.p) cudaFree(s->target.p);
   delete s;
   return LC_SUCCESS;
 }
@@ -134,6 +140,65 @@ lcError_t lcAttentionSessionForward(lcAttentionSession_t s, const void* q, const
                          s->dtype, &dev, stream);
   if (e != LC_SUCCESS) return e;
   return finish(s->b[3], out, pol.download_out, pol.synchronize, st);
+}
+
+// src/attention.cpp:12-38: the loss cadence when the policy leaves loss_every = 0.
+static int auto_loss_every(size_t seq, size_t d) {
+  if (seq == 256 && d == 64) return 32;
+  if (seq == 256 && d == 128) return 16;
+  if ((seq == 512 || seq == 1024) && (d == 64 || d == 128)) return 8;
+  return 4;
+}
+
+lcError_t lcAttentionSessionTrainStep(lcAttentionSession_t s, const float* q, const float* k, float* v,
+                                      const float* target, float* out, float learning_rate, float* loss_out,
+                                      const lcAttentionIoPolicy* policy, lcStream_t stream) {
+  if (!s || !(learning_rate > 0.0f)) return LC_INVALID_VALUE;
+  if (s->dtype != LC_DTYPE_F32) return LC_NOT_SUPPORTED;
+  std::lock_guard<std::mutex> lk(s->mu);
+  const lcAttentionIoPolicy pol = policy ? *policy : s->def;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!s->target.p) {
+    s->target.bytes = s->b[0].bytes;
+    if (cudaMalloc(&s->target.p, s->target.bytes) != cudaSuccess) {
+      s->target.p = nullptr;
+      return LC_OUT_OF_MEMORY;
+    }
+  }
+  lcError_t e;
+  if ((e = upload(s->b[0], q, pol.upload_q, st)) != LC_SUCCESS) return e;
+  if ((e = upload(s->b[1], k, pol.upload_k, st)) != LC_SUCCESS) return e;
+  if ((e = upload(s->b[2], v, pol.upload_v, st)) != LC_SUCCESS) return e;
+  if ((e = upload(s->target, target, pol.upload_target, st)) != LC_SUCCESS) return e;
+  bool take_loss = false;
+  if (loss_out) {
+    const int every = pol.loss_every == 0 ? auto_loss_every(s->seq, s->head_dim) : (pol.loss_every < 1 ? 1 : pol.loss_every);
+    take_loss = (s->train_steps % static_cast<size_t>(every)) == 0;
+  }
+  std::vector<float> loss(s->units);
+  lcAttentionIoPolicy dev;
+  lcAttentionIoPolicyDefault(&dev);
+  dev.upload_q = dev.upload_k = dev.upload_v = dev.upload_target = 0;
+  dev.download_out = dev.download_v = dev.synchronize = 0;
+  e = lcAttentionTrainStep(static_cast<const float*>(s->b[0].p), static_cast<const float*>(s->b[1].p),
+                           static_cast<float*>(s->b[2].p), static_cast<const float*>(s->target.p),
+                           static_cast<float*>(s->b[3].p), learning_rate, s->units, s->seq, s->head_dim, s->causal,
+                           take_loss ? loss.data() : nullptr, &dev, stream);
+  if (e != LC_SUCCESS) return e;
+  if (pol.download_v) {
+    if (!v) return LC_INVALID_VALUE;
+    if (cudaMemcpyAsync(v, s->b[2].p, s->b[2].bytes, cudaMemcpyDeviceToHost, st) != cudaSuccess) return LC_DRIVER_ERROR;
+  }
+  if ((e = finish(s->b[3], out, pol.download_out, pol.synchronize || pol.download_v, st)) != LC_SUCCESS) return e;
+  if (loss_out) {
+    if (take_loss) {
+      s->last_loss = loss;
+      s->has_last_loss = true;
+    }
+    for (size_t u = 0; u < s->units; ++u) loss_out[u] = s->has_last_loss ? s->last_loss[u] : 0.0f;
+  }
+  ++s->train_steps;
+  return LC_SUCCESS;
 }
 
 lcError_t lcMatMulSessionCreate(lcMatMulSession_t* out, size_t m, size_t k, size_t n, lcDataType dtype) {

@@ -111,6 +111,8 @@ _SIGS = {
     "lcMatMulSessionBuffer": (_i, [_vp, _i, C.POINTER(_vp)]),
     "lcMatMulSessionRun": (_i, [_vp, _vp, _vp, _vp, C.POINTER(MatMulIoPolicy), _vp]),
     "lcMatMulSessionRunBatch": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
+    "lcAttentionTrainStep": (_i, [_vp] * 5 + [_f, _sz, _sz, _sz, _i, _vp, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcAttentionSessionTrainStep": (_i, [_vp] * 6 + [_f, _vp, C.POINTER(AttentionIoPolicy), _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -448,6 +450,18 @@ class AttentionSession:
         lib.lcDeviceSynchronize()
         return out
 
+    def train_step(self, q, k, v, target, learning_rate: float, policy: AttentionIoPolicy = None):
+        """AttentionSession::trainStep (src/attention.cpp:285-343): returns (out, loss).  With the
+        default policy q/k/v/target are uploaded each call; pass a policy with upload_v = 0 to keep
+        training the session's resident v."""
+        out = np.empty(self.shape, np.float32)
+        loss = np.zeros(max(1, self.shape[0] if len(self.shape) == 3 else 1), np.float32)
+        arrs = [None if x is None else np.ascontiguousarray(x, dtype=np.float32) for x in (q, k, v, target)]
+        pol = policy if policy is not None else default_attention_policy()
+        check(lib.lcAttentionSessionTrainStep(self.h, *[_vp(x) for x in arrs], _vp(out), learning_rate,
+                                              _vp(loss), C.byref(pol), None), "train_step")
+        return out, (float(loss[0]) if loss.size == 1 else loss)
+
     def buffer(self, which: int) -> int:
         p = C.c_void_p()
         check(lib.lcAttentionSessionBuffer(self.h, which, C.byref(p)))
@@ -516,3 +530,19 @@ class MatMulResidentSession:
             self.close()
         except Exception:
             pass
+
+
+def attention_train_step(q, k, v, target, learning_rate: float, causal: bool = False):
+    """attentionTrainStep (src/attention.cpp:203-214) on the GPU: returns (out, updated v, loss).
+    q/k/v/target: [seq, d] or [units, seq, d] float32; loss per unit for batched input."""
+    q, k, t = (np.ascontiguousarray(x, dtype=np.float32) for x in (q, k, target))
+    v = np.array(v, dtype=np.float32, copy=True, order="C")
+    shape = q.shape
+    units = shape[0] if q.ndim == 3 else 1
+    seq, d = shape[-2], shape[-1]
+    out = np.empty_like(q)
+    loss = np.zeros(units, np.float32)
+    pol = default_attention_policy()
+    check(lib.lcAttentionTrainStep(_vp(q), _vp(k), _vp(v), _vp(t), _vp(out), learning_rate, units, seq, d,
+                                   int(causal), _vp(loss), C.byref(pol), None), "attention_train_step")
+    return out, v, (float(loss[0]) if q.ndim == 2 else loss)

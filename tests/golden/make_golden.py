@@ -99,6 +99,14 @@ def main():
     bias = rng.standard_normal(7).astype(np.float32)
     out["conv_stride2_pad0"] = dict(x=x, w=w, bias=bias, out=R.conv2d(x, w, bias, (2, 1), (0, 1), True))
 
+    # train step (src/attention_cpu.cpp:114-163)
+    rng = np.random.default_rng(6)
+    q, k, v, t = (rng.standard_normal((64, 32)).astype(np.float32) for _ in range(4))
+    for causal in (0, 1):
+        o2, v2, loss = R.attention_train_step(q, k, v, t, 0.1, causal=bool(causal))
+        out[f"train_step_64x32_c{causal}"] = dict(q=q, k=k, v=v, target=t, lr=np.float32(0.1), out=o2, v_new=v2,
+                                                  loss=np.float32(loss))
+
     for name, d in out.items():
         np.savez(os.path.join(HERE, f"{name}.npz"), **d)
     print(f"wrote {len(out)} fixtures to {HERE}")

@@ -109,3 +109,12 @@ def test_port_matches_reference_random(P):
     a = rng.uniform(-1, 1, (33, 70)).astype(np.float32)
     b = rng.uniform(-1, 1, (70, 19)).astype(np.float32)
     np.testing.assert_array_equal(R.matmul(a, b), P.matmul(a, b))
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_train_step_golden(P, causal):
+    g = golden(f"train_step_64x32_c{causal}")
+    out, v_new, loss = P.attention_train_step(g["q"], g["k"], g["v"], g["target"], float(g["lr"]), bool(causal))
+    close_enough(g["out"], out, 1e-5, 1e-5)
+    close_enough(g["v_new"], v_new, 1e-5, 1e-5)
+    assert abs(loss - float(g["loss"])) <= 1e-5 * abs(float(g["loss"])) + 1e-6
