@@ -257,6 +257,16 @@ lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, const float
 lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataType dtype,
                       const lcVectorAddIoPolicy* policy, lcStream_t stream);
 
+/* ops::matrixSub / matrixDiv (include/lightning_core/core/ops.hpp:31-49, CPU
+ * src/ops/matrix_elemwise.cpp:8-29): out = a - b / a / b elementwise over rows x cols, f32 or f64,
+ * IEEE arithmetic (sub is bit-identical to the reference CPU loop; the reference's -ffast-math
+ * build divides approximately, so div agrees to rounding).  The policy struct has the fields of
+ * the reference's MatrixElementwiseIoPolicy (ops/policy.hpp:15-20). */
+lcError_t lcMatrixSub(const void* a, const void* b, void* out, size_t rows, size_t cols, lcDataType dtype,
+                      const lcVectorAddIoPolicy* policy, lcStream_t stream);
+lcError_t lcMatrixDiv(const void* a, const void* b, void* out, size_t rows, size_t cols, lcDataType dtype,
+                      const lcVectorAddIoPolicy* policy, lcStream_t stream);
+
 /* (x - mean)/sqrt(var + eps) over the last axis, population variance, no affine
  * (the reference's LN formula, README.md:2267-2270).  Device pointers, fp32. */
 lcError_t lcLayerNorm(const float* x, float* out, size_t rows, size_t cols, float eps, lcStream_t stream);

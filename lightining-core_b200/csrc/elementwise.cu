@@ -3,6 +3,8 @@
 // vector_add replaces src/ops/vector_add_cuda.cu:12-86 of the reference (a scalar grid-stride
 // add followed by cudaDeviceSynchronize): 128-bit loads/stores, 4 independent vectors in flight
 // per thread, grid sized to a multiple of the SM count, stream-ordered with no device sync.
+// matrix_sub / matrix_div (src/ops/matrix_elemwise.cpp:8-29) are the same kernel with another
+// operator (IEEE subtraction and division).
 // layer_norm restates the reference's LN formula (README.md:2267-2270): per row of the last
 // axis, (x - mean) / sqrt(var + eps), population variance, no affine; one warp per row, two
 // passes over the row held in registers (mean first, then centred variance).
@@ -13,9 +15,23 @@
 namespace lcb {
 namespace {
 
-template <typename V, typename S, int PER>
+struct OpAdd {
+  template <typename S>
+  __device__ __forceinline__ S operator()(S x, S y) const { return x + y; }
+};
+struct OpSub {
+  template <typename S>
+  __device__ __forceinline__ S operator()(S x, S y) const { return x - y; }
+};
+struct OpDiv {
+  template <typename S>
+  __device__ __forceinline__ S operator()(S x, S y) const { return x / y; }
+};
+
+template <typename V, typename S, int PER, class Op = OpAdd>
 __global__ void __launch_bounds__(256) vadd_kernel(const S* __restrict__ a, const S* __restrict__ b,
                                                    S* __restrict__ out, size_t n) {
+  const Op op;
   constexpr int L = sizeof(V) / sizeof(S);
   const size_t nv = n / L;
   const V* av = reinterpret_cast<const V*>(a);
@@ -37,7 +53,7 @@ __global__ void __launch_bounds__(256) vadd_kernel(const S* __restrict__ a, cons
       const S* ys = reinterpret_cast<const S*>(&y[u]);
       S* zs = reinterpret_cast<S*>(&z);
 #pragma unroll
-      for (int e = 0; e < L; ++e) zs[e] = xs[e] + ys[e];
+      for (int e = 0; e < L; ++e) zs[e] = op(xs[e], ys[e]);
       __stcs(ov + i + u * stride, z);
     }
   }
@@ -47,25 +63,26 @@ __global__ void __launch_bounds__(256) vadd_kernel(const S* __restrict__ a, cons
     const S* ys = reinterpret_cast<const S*>(&y);
     S* zs = reinterpret_cast<S*>(&z);
 #pragma unroll
-    for (int e = 0; e < L; ++e) zs[e] = xs[e] + ys[e];
+    for (int e = 0; e < L; ++e) zs[e] = op(xs[e], ys[e]);
     ov[i] = z;
   }
   // Scalar tail (n not a multiple of the vector width), handled by the first threads.
   const size_t tail0 = nv * L;
   const size_t t = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
-  if (tail0 + t < n) out[tail0 + t] = a[tail0 + t] + b[tail0 + t];
+  if (tail0 + t < n) out[tail0 + t] = op(a[tail0 + t], b[tail0 + t]);
 }
 
-template <typename S>
+template <typename S, class Op = OpAdd>
 __global__ void vadd_scalar_kernel(const S* a, const S* b, S* out, size_t n) {
+  const Op op;
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    out[i] = a[i] + b[i];
+    out[i] = op(a[i], b[i]);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <typename V, typename S>
+template <typename V, typename S, class Op = OpAdd>
 cudaError_t vadd(const S* a, const S* b, S* out, size_t n, cudaStream_t s) {
   const int sms = device_ctx() ? device_ctx()->sm_count : 148;
   if (n == 0) return cudaSuccess;
@@ -76,9 +93,9 @@ cudaError_t vadd(const S* a, const S* b, S* out, size_t n, cudaStream_t s) {
     const size_t cap = static_cast<size_t>(sms) * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    vadd_kernel<V, S, 4><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, b, out, n);
+    vadd_kernel<V, S, 4, Op><<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, b, out, n);
   } else {
-    vadd_scalar_kernel<S><<<sms * 8, 256, 0, s>>>(a, b, out, n);
+    vadd_scalar_kernel<S, Op><<<sms * 8, 256, 0, s>>>(a, b, out, n);
   }
   return cudaGetLastError();
 }
@@ -152,6 +169,17 @@ cudaError_t vector_add_f32(const float* a, const float* b, float* out, size_t n,
 }
 cudaError_t vector_add_f64(const double* a, const double* b, double* out, size_t n, cudaStream_t s) {
   return vadd<double2, double>(a, b, out, n, s);
+}
+
+cudaError_t matrix_binary(int op, int f64, const void* a, const void* b, void* out, size_t n, cudaStream_t s) {
+  if (f64) {
+    const double *x = static_cast<const double*>(a), *y = static_cast<const double*>(b);
+    double* z = static_cast<double*>(out);
+    return op == 0 ? vadd<double2, double, OpSub>(x, y, z, n, s) : vadd<double2, double, OpDiv>(x, y, z, n, s);
+  }
+  const float *x = static_cast<const float*>(a), *y = static_cast<const float*>(b);
+  float* z = static_cast<float*>(out);
+  return op == 0 ? vadd<float4, float, OpSub>(x, y, z, n, s) : vadd<float4, float, OpDiv>(x, y, z, n, s);
 }
 
 cudaError_t layer_norm_f32(const float* x, float* out, size_t rows, size_t cols, float eps, cudaStream_t s) {

@@ -78,6 +78,8 @@ bool attention_bf16_tc_supported(const AttnArgs& a);
 // ---- elementwise ----------------------------------------------------------------------------
 cudaError_t vector_add_f32(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
 cudaError_t vector_add_f64(const double* a, const double* b, double* out, size_t n, cudaStream_t s);
+// op 0: a - b, op 1: a / b (f64 selects double).
+cudaError_t matrix_binary(int op, int f64, const void* a, const void* b, void* out, size_t n, cudaStream_t s);
 cudaError_t layer_norm_f32(const float* x, float* out, size_t rows, size_t cols, float eps, cudaStream_t s);
 
 }  // namespace lcb

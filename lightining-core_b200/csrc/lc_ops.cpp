@@ -429,3 +429,34 @@ extern "C" lcError_t lcAttentionTrainStep(const float* q, const float* k, float*
   if (synced) LC_TRY(cudaStreamSynchronize(s));
   return check_error_word(synced);
 }
+
+// ops::matrixSubWithPolicy / matrixDivWithPolicy (include/lightning_core/core/ops.hpp:31-49;
+// CPU src/ops/matrix_elemwise.cpp:8-29): out = a - b / a / b over rows x cols.
+static lcError_t matrix_op(int op, const void* a, const void* b, void* out, size_t rows, size_t cols,
+                           lcDataType dtype, const lcVectorAddIoPolicy* policy, lcStream_t stream) {
+  if (!a || !b || !out || rows == 0 || cols == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_F64) return LC_NOT_SUPPORTED;
+  lcVectorAddIoPolicy pol = {0, 0, 0, 0};
+  if (policy) pol = *policy;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t n = rows * cols, bytes = n * elem_size(dtype);
+  const void *da, *db;
+  void* dc;
+  LC_TRY(io.in(a, bytes, pol.upload_a, &da));
+  LC_TRY(io.in(b, bytes, pol.upload_b, &db));
+  LC_TRY(io.out(out, bytes, pol.download_out, &dc));
+  trace_op(op == 0 ? kOpMatrixSub : kOpMatrixDiv, n);
+  LC_TRY(matrix_binary(op, dtype == LC_DTYPE_F64, da, db, dc, n, io.stream()));
+  LC_TRY(io.finish(out, dc, bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+extern "C" lcError_t lcMatrixSub(const void* a, const void* b, void* out, size_t rows, size_t cols, lcDataType dtype,
+                                 const lcVectorAddIoPolicy* policy, lcStream_t stream) {
+  return matrix_op(0, a, b, out, rows, cols, dtype, policy, stream);
+}
+
+extern "C" lcError_t lcMatrixDiv(const void* a, const void* b, void* out, size_t rows, size_t cols, lcDataType dtype,
+                                 const lcVectorAddIoPolicy* policy, lcStream_t stream) {
+  return matrix_op(1, a, b, out, rows, cols, dtype, policy, stream);
+}

@@ -93,6 +93,8 @@ _SIGS = {
     "lcRuntimeTraceCount": (_sz, []),
     "lcRuntimeTraceCapacity": (_sz, []),
     "lcRuntimeTraceGet": (_i, [_sz, C.POINTER(RuntimeTraceEvent)]),
+    "lcMatrixSub": (_i, [_vp, _vp, _vp, _sz, _sz, _i, C.POINTER(VectorAddIoPolicy), _vp]),
+    "lcMatrixDiv": (_i, [_vp, _vp, _vp, _sz, _sz, _i, C.POINTER(VectorAddIoPolicy), _vp]),
     "lcTuneCacheLoad": (_i, [_i, C.c_char_p]),
     "lcTuneCacheSave": (_i, [_i, C.c_char_p]),
     "lcTuneCacheReset": (_i, [_i]),
@@ -391,6 +393,30 @@ def vector_add(a, b, device="cuda"):
     check(lib.lcVectorAdd(_vp(a), _vp(b), _vp(out), a.size, F32 if a.dtype == np.float32 else F64, C.byref(pol),
                           None), "vector_add")
     return out
+
+
+def _matrix_op(fn, name, a, b, rows, cols, device):
+    _parse_device(device)
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b)
+    if a.size != rows * cols or b.size != rows * cols or a.dtype != b.dtype or a.dtype not in (np.float32,
+                                                                                            np.float64):
+        raise ValueError(f"{name}: a and b must be float32/float64 arrays of rows*cols elements")
+    out = np.empty_like(a)
+    pol = VectorAddIoPolicy()
+    lib.lcVectorAddIoPolicyDefault(C.byref(pol))
+    check(fn(_vp(a), _vp(b), _vp(out), rows, cols, F32 if a.dtype == np.float32 else F64, C.byref(pol), None), name)
+    return out
+
+
+def matrix_sub(a, b, rows, cols, device="cuda"):
+    """bind_ops.cpp:1126-1160: out = a - b over rows x cols."""
+    return _matrix_op(lib.lcMatrixSub, "matrix_sub", a, b, rows, cols, device)
+
+
+def matrix_div(a, b, rows, cols, device="cuda"):
+    """out = a / b over rows x cols (IEEE division)."""
+    return _matrix_op(lib.lcMatrixDiv, "matrix_div", a, b, rows, cols, device)
 
 
 def layer_norm(x, eps=1e-5):

@@ -298,6 +298,14 @@ void orc_vector_add(const float* a, const float* b, float* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = a[i] + b[i];
 }
 
+void orc_matrix_sub(const float* a, const float* b, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = a[i] - b[i];
+}
+
+void orc_matrix_div(const float* a, const float* b, float* out, size_t n) {
+  for (size_t i = 0; i < n; ++i) out[i] = a[i] / b[i];
+}
+
 /* README.md:2267-2270: mean and population variance over the last axis (numpy computes both
  * in float32 with pairwise sums; accumulated in double here, which is within fp32 rounding). */
 void orc_layer_norm(const float* x, float* out, size_t rows, size_t cols, float eps) {

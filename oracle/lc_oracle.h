@@ -52,6 +52,9 @@ int orc_conv_attention_images(const float* x, const float* w, const float* bias,
 
 /* src/ops/vector_add_cpu.cpp:13-43 (scalar semantics). */
 void orc_vector_add(const float* a, const float* b, float* out, size_t n);
+/* src/ops/matrix_elemwise.cpp:8-29: out = a - b / a / b. */
+void orc_matrix_sub(const float* a, const float* b, float* out, size_t n);
+void orc_matrix_div(const float* a, const float* b, float* out, size_t n);
 /* README.md:2267-2270 _layer_norm_np: (x - mean) / sqrt(var + eps), population variance, last axis. */
 void orc_layer_norm(const float* x, float* out, size_t rows, size_t cols, float eps);
 

@@ -46,6 +46,8 @@ class _Lib:
             "attention_train_step": [_f, _f, _f, _f, _f, C.c_float, _sz, _sz, C.c_int, _f],
         }
         if pfx == "ref":
+            sig["matrix_sub"] = [_f, _f, _f, _sz, _sz]
+            sig["matrix_div"] = [_f, _f, _f, _sz, _sz]
             sig["attention_forward_units"] = [_f, _f, _f, _f, _sz, _sz, _sz, C.c_int, C.c_int]
             sig["conv_attention_images"] = [_f, _f, _f, _f, _f] + [_sz] * 14 + [C.c_int]
         else:
@@ -54,10 +56,13 @@ class _Lib:
             sig["conv_attention_images"] = [_f, _f, _f, _f, _f] + [_sz] * 14 + [C.c_int]
             sig["layer_norm"] = [_f, _f, _sz, _sz, C.c_float]
             sig["bf16_round_array"] = [_f, _f, _sz]
+            sig["matrix_sub"] = [_f, _f, _f, _sz]
+            sig["matrix_div"] = [_f, _f, _f, _sz]
         for name, args in sig.items():
             fn = getattr(L, f"{pfx}_{name}")
             fn.argtypes = args
-            fn.restype = C.c_int if name not in ("vector_add", "layer_norm", "bf16_round_array") or pfx == "ref" else None
+            fn.restype = C.c_int if name not in ("vector_add", "layer_norm", "bf16_round_array", "matrix_sub",
+                                                 "matrix_div") or pfx == "ref" else None
 
     def _call(self, name, *args):
         return getattr(self.lib, f"{self.prefix}_{name}")(*args)
@@ -143,6 +148,16 @@ class _Lib:
     def vector_add(self, a, b):
         out = np.zeros_like(a)
         self._call("vector_add", _p(a), _p(b), _p(out), a.size)
+        return out
+
+    def matrix_op(self, op, a, b):
+        out = np.zeros_like(a)
+        if self.prefix == "ref":
+            rc = self._call(f"matrix_{op}", _p(a), _p(b), _p(out), a.shape[0], a.size // a.shape[0])
+            if rc:
+                raise RuntimeError(f"matrix_{op} rc={rc}")
+        else:
+            self._call(f"matrix_{op}", _p(a), _p(b), _p(out), a.size)
         return out
 
     def layer_norm(self, x, eps=1e-5):

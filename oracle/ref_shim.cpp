@@ -156,6 +156,14 @@ int ref_conv_attention_images(const float* x, const float* w, const float* bias,
   });
 }
 
+int ref_matrix_sub(const float* a, const float* b, float* out, std::size_t rows, std::size_t cols) {
+  return st(lc::ops::matrixSub<float>(a, b, out, rows, cols, lc::runtime::Device::kCPU));
+}
+
+int ref_matrix_div(const float* a, const float* b, float* out, std::size_t rows, std::size_t cols) {
+  return st(lc::ops::matrixDiv<float>(a, b, out, rows, cols, lc::runtime::Device::kCPU));
+}
+
 int ref_vector_add(const float* a, const float* b, float* out, std::size_t n) {
   return st(lc::ops::vectorAdd<float>(a, b, out, n, lc::runtime::Device::kCPU));
 }

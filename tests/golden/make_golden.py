@@ -54,6 +54,11 @@ def main():
     a = make_vec(257, 0.005, 0.2)
     b = make_vec(257, 0.003, -0.1)
     out["parity_vector_add"] = dict(a=a, b=b, out=R.vector_add(a, b))
+    # tests/test_backend_parity.cpp:113-155 (b pushed away from zero as there)
+    a = make_vec(9 * 13, 0.01, 0.7).reshape(9, 13)
+    b = make_vec(9 * 13, 0.008, 0.5).reshape(9, 13)
+    b = np.where(np.abs(b) < 0.1, np.where(b < 0, -0.1, 0.1), b).astype(np.float32)
+    out["parity_matrix_ops"] = dict(a=a, b=b, sub=R.matrix_op("sub", a, b), div=R.matrix_op("div", a, b))
     q = make_vec(16 * 32, 0.01).reshape(16, 32)
     k = make_vec(16 * 32, 0.009, 0.02).reshape(16, 32)
     v = make_vec(16 * 32, 0.008, -0.01).reshape(16, 32)

@@ -226,3 +226,20 @@ def test_attention_bf16_stress_vs_torch_fp32(gpu, units, s, d, causal):
     ref = torch.nn.functional.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=bool(causal))
     err = (o.float() - ref).abs()
     assert bool((err <= 2e-2 + 2e-2 * ref.abs()).all()), float(err.max())
+
+
+def test_matrix_sub_div(gpu):
+    # tests/test_backend_parity.cpp:113-155 inputs and tolerances (sub exact; div 2e-4, as the
+    # reference's -ffast-math build divides approximately while the GPU divides in IEEE)
+    g = golden("parity_matrix_ops")
+    np.testing.assert_array_equal(gpu.matrix_sub(g["a"], g["b"], 9, 13), g["sub"])
+    close_enough(g["div"], gpu.matrix_div(g["a"], g["b"], 9, 13), 2e-4, 2e-4)
+    rng = np.random.default_rng(12)
+    for rows, cols in ((1, 1), (3, 1027), (1024, 1024)):
+        a = rng.uniform(-1, 1, (rows, cols)).astype(np.float32)
+        b = rng.uniform(0.5, 2, (rows, cols)).astype(np.float32)
+        np.testing.assert_array_equal(gpu.matrix_sub(a, b, rows, cols), a - b)
+        np.testing.assert_array_equal(gpu.matrix_div(a, b, rows, cols), a / b)
+    a = rng.uniform(-1, 1, 999)
+    b = rng.uniform(0.5, 2, 999)
+    np.testing.assert_array_equal(gpu.matrix_div(a, b, 9, 111), a / b)

@@ -118,3 +118,10 @@ def test_train_step_golden(P, causal):
     close_enough(g["out"], out, 1e-5, 1e-5)
     close_enough(g["v_new"], v_new, 1e-5, 1e-5)
     assert abs(loss - float(g["loss"])) <= 1e-5 * abs(float(g["loss"])) + 1e-6
+
+
+def test_matrix_ops_golden(P):
+    g = golden("parity_matrix_ops")
+    np.testing.assert_array_equal(P.matrix_op("sub", g["a"], g["b"]), g["sub"])
+    # the reference build (-ffast-math) divides approximately; its own parity tolerance is 2e-4
+    close_enough(g["div"], P.matrix_op("div", g["a"], g["b"]), 2e-4, 2e-4)
