@@ -400,6 +400,23 @@ def extra_configs(args, lc, torch, dev, sp):
                                                        192, 3, 3, 1, 1, 1, 1, 3136, 64, 64, 1, None, sp)), 3)
     flops = 2 * 32 * 3136 * 192 * 576 + 32 * 4 * 3136 ** 2 * 64 + 2 * 32 * 3136 * 64 * 64
     res["cfg5_conv_attention_f32"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12}
+    del x, out
+    # HBM-bound elementwise ops against the measured copy bandwidth (inputs >> L2).
+    pk, pk_kind = peaks()
+    hbm = float(pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    n = 1 << 28
+    va, vb = torch.rand(n, device=dev), torch.rand(n, device=dev)
+    vc = torch.empty_like(va)
+    ms = timeit(lambda: lc.check(L.lcVectorAdd(ptr(va), ptr(vb), ptr(vc), n, lc.F32, None, sp)), 10)
+    gbs = 12.0 * n / (ms * 1e-3) / 1e9
+    res["vector_add_f32_2^28"] = {"ms": ms, "gbs": gbs, "frac_of_hbm": gbs / hbm, "hbm_peak": f"{hbm} ({pk_kind})"}
+    del va, vb, vc
+    rows, cols = 65536, 1024
+    x = torch.randn((rows, cols), device=dev)
+    y = torch.empty_like(x)
+    ms = timeit(lambda: lc.check(L.lcLayerNorm(ptr(x), ptr(y), rows, cols, 1e-5, sp)), 10)
+    gbs = 8.0 * rows * cols / (ms * 1e-3) / 1e9
+    res["layer_norm_f32_65536x1024"] = {"ms": ms, "gbs": gbs, "frac_of_hbm": gbs / hbm}
     return res
 
 
