@@ -10,12 +10,14 @@
 //               so a late V slot never holds back K); L2 prefetch of upcoming tiles; 3-D tensor
 //               maps [units, S, D] so rows past S read as zero; 128-byte swizzle.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1}
-//               overlaps the softmax of S_j), then O += P_j V_j once P_j is in shared memory.
+//               overlaps the softmax of S_j), then O += P_j V_j with P_j read from TMEM (the A
+//               operand of tcgen05.mma may live in tensor memory).
 //   warps 2..5  softmax + epilogue: each thread owns one query row (= one TMEM lane), so row
 //               max and sum need no shuffles.  Scores are scaled into the log2 domain; O is
 //               rescaled in TMEM only when the running max grows by more than 8 (2^8), which
-//               keeps exp2 values <= 256 and the final O / l exact.  P is written as bf16 in
-//               the UMMA K-major 128-byte-swizzled layout.  The epilogue divides by l, applies
+//               keeps exp2 values <= 256 and the final O / l exact.  P_j is written as packed
+//               bf16 pairs over the first 32 columns of S_j's own TMEM buffer (tcgen05.st), so
+//               it never touches shared memory.  The epilogue divides by l, applies
 //               the postprocess and stores bf16.
 // Causal: only KV tiles at or below the diagonal are visited; per-element masks only on the
 // diagonal / sequence-tail tile.  CTAs run unit by unit (heaviest Q tile first inside a unit), so
@@ -43,8 +45,8 @@ constexpr int TK = 64;                  // keys per KV tile
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
 constexpr int KCHUNK_BYTES = TK * 128;  // one [64 rows x 64 bf16] swizzled box = 8 KB
 constexpr int K_STAGES = 2;  // K_{j+2} loads as soon as S_j is done
-constexpr int V_STAGES = 1;  // V_{j+1} loads once PV_j is done (a separate producer thread)
-constexpr int P_BUFS = 2;     // P_j goes to buffer j%2, so softmax j never waits for PV_{j-1}
+constexpr int V_STAGES = 2;  // V_{j+2} loads once PV_j is done (a separate producer thread)
+constexpr int P_BUFS = 2;    // P_j aliases TMEM score buffer j%2
 constexpr int NUM_THREADS = 224;  // 7 warps: K/Q loader, MMA, 4 softmax, V loader
 constexpr uint32_t TMEM_COLS = 256;  // S buffers at 0 and 64, O at 128: two CTAs fit one SM
 constexpr float LOG2E = 1.4426950408889634f;
@@ -67,12 +69,10 @@ struct Layout {
   static constexpr int NCH = D / 64;                      // 64-column chunks per row
   static constexpr int Q_BYTES = NCH * CHUNK_BYTES;
   static constexpr int KV_BYTES = NCH * KCHUNK_BYTES;
-  static constexpr int P_BYTES = CHUNK_BYTES;              // 128 rows x 64 keys = 1 chunk
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + K_STAGES * KV_BYTES;
-  static constexpr int P_OFF = V_OFF + V_STAGES * KV_BYTES;
-  static constexpr int TAIL_OFF = P_OFF + P_BUFS * P_BYTES;
+  static constexpr int TAIL_OFF = V_OFF + V_STAGES * KV_BYTES;
   // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel
   // without static shared memory starts 1 KB-aligned; the kernel checks this and bails out
   // with an error code otherwise.
@@ -122,10 +122,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast, so the warp stays
 // converged for the .sync.aligned tcgen05 loads that follow even on the abort path.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* err,
@@ -158,7 +154,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   uint8_t* sQ = smem + LY::Q_OFF;
   uint8_t* sK = smem + LY::K_OFF;
   uint8_t* sV = smem + LY::V_OFF;
-  uint8_t* sP = smem + LY::P_OFF;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -240,9 +235,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const int vs = j % V_STAGES;
         if (j + V_STAGES < n_kv)
           for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
-        // The single V buffer last held V_{j-1}: PV_{j-1} (one commit: o_done[(j-1)%2]) must be done.
-        if (j >= V_STAGES && !mbar_wait_bounded(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag,
-                                                p.err_word, kErrAttnLoadWait)) {
+        // Slot vs last held V_{j-2}: PV_{j-2} (one commit: o_done[j%2]) must be done.  PV_j cannot
+        // complete before V_j is issued here, so the parity wait is unambiguous.
+        if (j >= V_STAGES && !mbar_wait_bounded(&st->o_done[(j - V_STAGES) % P_BUFS], ((j - V_STAGES) >> 1) & 1,
+                                                abort_flag, p.err_word, kErrAttnLoadWait)) {
           ok = false;
           break;
         }
@@ -258,9 +254,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TK, 0, 0);    // Q K-major, K K-major
-      constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P K-major, V MN-major
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P (TMEM) K-major, V MN-major
       const uint32_t q_addr = smem_u32(sQ);
-      const uint32_t p_addr = smem_u32(sP);
       bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
@@ -298,11 +293,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const uint32_t o_tmem = tmem + 2 * TK;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
-          // A = P (keys are K): +32 B per 16 keys.  B = V, MN-major: 64-column d chunks 8 KB apart
-          // (LBO), +16 key rows * 128 B per step.
-          const uint64_t adesc = smem_desc_sw128(p_addr + (j % P_BUFS) * LY::P_BYTES + kk * 32, 16, 1024);
+          // A = P_j in TMEM (lanes = rows, 2 keys per column): +8 columns per 16 keys.  B = V,
+          // MN-major: 64-column d chunks 8 KB apart (LBO), +16 key rows * 128 B per step.
+          const uint32_t a_tmem = tmem + static_cast<uint32_t>((j % P_BUFS) * TK + kk * 8);
           const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, KCHUNK_BYTES, 1024);
-          umma_f16_ss(o_tmem, adesc, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(o_tmem, a_tmem, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&st->o_done[j % P_BUFS]);  // the only commit of this MMA group
       }
@@ -355,15 +350,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
                                 __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31]));
       const float mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
                        p.scale_log2;
-      // P buffer j%2 was last read by PV_{j-2}.  o_done[j%2] completes once per use of that buffer
-      // and PV_j cannot complete before P_j exists, so this parity wait is unambiguous.
-      if (j >= 2) {
-        if (!warp_wait(&st->o_done[j % P_BUFS], ((j - 2) >> 1) & 1, abort_flag, p.err_word,
-                       kErrAttnCorrectionWait)) {
-          ok = false;
-          break;
-        }
-      }
+      // P_j overwrites S_j in place.  The last reader of those columns before S_j was PV_{j-2},
+      // issued before S_j by the same thread; s_full[j&1] therefore already covers it.
       const bool need = mx > m + RESCALE_THRESHOLD;
       float factor = 1.0f;
       if (need) {
@@ -394,23 +382,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       // visible, so the first tile sets it).  8 partial sums keep the adds independent.
       const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
       uint64_t ps2[4] = {0, 0, 0, 0};  // 4 independent packed partial sums
-      uint8_t* prow = sP + (j % P_BUFS) * Layout<D>::P_BYTES + row * 128;
+      const uint32_t p_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TK);
 #pragma unroll
-      for (int g = 0; g < TK / 8; ++g) {
-        uint32_t w[4];
+      for (int g = 0; g < TK / 32; ++g) {
+        uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int e = g * 8 + 2 * i;
+        for (int i = 0; i < 16; ++i) {
+          const int e = g * 32 + 2 * i;
           // x = s*scale - m for two scores at once; masked scores are -inf, so ex2 gives 0.
           float x0, x1;
           unpk2(fma2(pk2(__uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31])),
                      sc2, nm2),
                 x0, x1);
           const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
-          ps2[i] = add2(ps2[i], pk2(e0, e1));
+          ps2[i & 3] = add2(ps2[i & 3], pk2(e0, e1));
           w[i] = pack_bf16x2(e0, e1);
         }
-        *reinterpret_cast<uint4*>(prow + ((g ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        tmem_st16(p_tmem + g * 16, w);
       }
       float sum;
       {
@@ -420,7 +408,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         sum = a + b;
       }
       l += sum;
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&st->p_full);
