@@ -18,7 +18,8 @@
 //               keeps exp2 values <= 256 and the final O / l exact.  P_j is written as packed
 //               bf16 pairs over the first 32 columns of S_j's own TMEM buffer (tcgen05.st), so
 //               it never touches shared memory.  The epilogue divides by l, applies
-//               the postprocess and stores bf16.
+//               the postprocess, stages bf16 O in the (by then idle) Q buffer and writes it with
+//               TMA stores.
 // Causal: only KV tiles at or below the diagonal are visited; per-element masks only on the
 // diagonal / sequence-tail tile.  CTAs run unit by unit (heaviest Q tile first inside a unit), so
 // a wave of CTAs shares the K/V of few units in L2.
@@ -60,6 +61,7 @@ struct AttnTail {
   uint64_t p_full;
   uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
   uint64_t drain;
+  uint64_t o_staged;  // the 4 softmax warps have written the bf16 O tile into the Q buffer
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -141,7 +143,8 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, 
 template <int D>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                  const __grid_constant__ CUtensorMap map_v, const FaParams p) {
+                  const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                  const FaParams p) {
   using LY = Layout<D>;
   constexpr int NCH = LY::NCH;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -174,11 +177,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     mbar_init(&st->o_done[0], 1);
     mbar_init(&st->o_done[1], 1);
     mbar_init(&st->drain, 1);
+    mbar_init(&st->o_staged, 4);
     st->abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
     tma_prefetch_desc(&map_v);
+    tma_prefetch_desc(&map_o);
+    // The Q tile (a cold HBM read) is requested before the TMEM allocation and the CTA barrier.
+    mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
+    load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
   }
   if (warp == 0) {
     tmem_alloc(&st->tmem_base, TMEM_COLS);
@@ -200,8 +208,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // ------------------------------------------------------------ TMA producer: Q and K
     if (lane == 0) {
       bool ok = true;
-      mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
-      load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
       int k_issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int ks = j % K_STAGES;
@@ -420,36 +426,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     if (ok && warp_wait(&st->o_done[(n_kv - 1) % P_BUFS], ((n_kv - 1) >> 1) & 1, abort_flag, p.err_word,
                         kErrAttnCorrectionWait)) {
       tc_fence_after();
+      // Epilogue: O / l (+ postprocess) as bf16 into the Q buffer, which no MMA reads any more
+      // (every S MMA completed before the last P.V), in the 128-byte-swizzled layout of the Q
+      // tile (16-byte chunk k of row r at chunk k ^ (r & 7): conflict-free), then one TMA store
+      // per 64-column box.  Rows past the sequence end are clipped by the tensor map.
       const float inv = 1.0f / l;
-      __nv_bfloat16* orow = p.out + (static_cast<long long>(unit) * p.seq + qrow) * D;
-#pragma unroll 1
-      for (int c = 0; c < D; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(o_tmem + c, r);
-        tmem_wait_ld();
-        float x[16];
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + c, r);
+        uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float y = __uint_as_float(r[e]) * inv;
+          float y0 = __uint_as_float(r[2 * e]) * inv, y1 = __uint_as_float(r[2 * e + 1]) * inv;
           if (p.post) {
-            y = y * p.post_scale + p.post_bias;
-            if (p.post_relu && y < 0.0f) y = 0.0f;
+            y0 = y0 * p.post_scale + p.post_bias;
+            y1 = y1 * p.post_scale + p.post_bias;
+            if (p.post_relu) {
+              y0 = fmaxf(y0, 0.0f);
+              y1 = fmaxf(y1, 0.0f);
+            }
           }
-          x[e] = y;
+          w[e] = pack_bf16x2(y0, y1);
         }
-        if (qrow < p.seq) {
-          uint4 a, b;
-          a.x = pack_bf16x2(x[0], x[1]);
-          a.y = pack_bf16x2(x[2], x[3]);
-          a.z = pack_bf16x2(x[4], x[5]);
-          a.w = pack_bf16x2(x[6], x[7]);
-          b.x = pack_bf16x2(x[8], x[9]);
-          b.y = pack_bf16x2(x[10], x[11]);
-          b.z = pack_bf16x2(x[12], x[13]);
-          b.w = pack_bf16x2(x[14], x[15]);
-          reinterpret_cast<uint4*>(orow + c)[0] = a;
-          reinterpret_cast<uint4*>(orow + c)[1] = b;
+        uint8_t* srow = sQ + (c >> 6) * CHUNK_BYTES + row * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int ch = ((c & 63) >> 3) + i;
+          *reinterpret_cast<uint4*>(srow + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->o_staged);
+      if (warp == 2 && lane == 0 &&
+          mbar_wait_bounded(&st->o_staged, 0, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+        for (int c = 0; c < NCH; ++c) tma_store_3d(&map_o, sQ + c * CHUNK_BYTES, c * 64, q0, unit);
+        bulk_commit_group();
+        bulk_wait_group_read0();  // shared memory must outlive the store's reads
       }
     }
   }
@@ -483,9 +498,9 @@ template <int D>
 cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D, TILE) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D, TK) ||
-      !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TK))
+      !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TK) || !make_tmap_heads(&mo, a.out, a.units, a.seq, D, TILE))
     return cudaErrorInvalidValue;
   static bool attr_set = false;  // benign race: idempotent
   if (!attr_set) {
@@ -510,7 +525,7 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   p.err_word = ctx->err_word;
   const long long blocks = static_cast<long long>(p.nq) * a.units;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D>::SMEM, s>>>(mq, mk, mv, p);
+  fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D>::SMEM, s>>>(mq, mk, mv, mo, p);
   return cudaGetLastError();
 }
 
