@@ -58,7 +58,7 @@ struct AttnTail {
   uint64_t k_full[K_STAGES];
   uint64_t v_full[V_STAGES];
   uint64_t s_full[2];
-  uint64_t p_full;
+  uint64_t p_full[2];       // p_full[b]: P_j with j%2 == b is in TMEM (4 warp arrivals)
   uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
   uint64_t drain;
   uint64_t o_staged;  // the 4 softmax warps have written the bf16 O tile into the Q buffer
@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     for (int s = 0; s < V_STAGES; ++s) mbar_init(&st->v_full[s], 1);
     mbar_init(&st->s_full[0], 1);
     mbar_init(&st->s_full[1], 1);
-    mbar_init(&st->p_full, 4);
+    mbar_init(&st->p_full[0], 4);
+    mbar_init(&st->p_full[1], 4);
     mbar_init(&st->o_done[0], 1);
     mbar_init(&st->o_done[1], 1);
     mbar_init(&st->drain, 1);
@@ -289,7 +290,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           ok = false;
           break;
         }
-        if (!mbar_wait_bounded(&st->p_full, j & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+        // One barrier per TMEM buffer: p_full[j&1] next completes for P_{j+2}, which needs S_{j+2},
+        // issued only after this wait, so the parity wait is unambiguous.  (A single barrier
+        // waited with parity j&1 could already have completed P_j and P_{j+1}.)
+        if (!mbar_wait_bounded(&st->p_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
             !mbar_wait_bounded(&st->v_full[s], (j / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
           ok = false;
           break;
@@ -417,7 +421,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&st->p_full);
+      if (lane == 0) mbar_arrive(&st->p_full[j & 1]);
     }
     // The last two PVs (one per P buffer) must have landed in O.
     if (ok && n_kv >= 2)

@@ -77,6 +77,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Bounded wait for threads whose wake-up latency is not critical (TMA producers): between polls
+// the thread sleeps `ns` nanoseconds, leaving issue slots to the warps that do the math.
+__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                          unsigned* err_word, unsigned code, unsigned ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    __nanosleep(ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > LC_WAIT_TIMEOUT_NS) {
+      *abort_flag = 1;
+      if (err_word) atomicCAS(err_word, 0u, code);
+      return false;
+    }
+  }
+}
+
 // Bounded wait.  `abort_flag` is a CTA-shared word: once any role of the CTA gives up, every
 // other wait returns false immediately.  Returns true when the phase completed.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
