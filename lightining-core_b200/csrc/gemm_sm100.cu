@@ -256,6 +256,250 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---- 2-SM variant ---------------------------------------------------------------------------
+// A cluster of two CTAs (two SMs) computes a 256x256 tile with tcgen05.mma.cta_group::2
+// (M=256, N=256, K=16): each CTA stages its own 128 rows of A and its own 128 columns of B, so
+// per SM the operand traffic is 2/3 of the 1-SM 128x256 tile and the 32 KB stages allow a
+// 6-deep ring.  The leader CTA (rank 0) arms the stage barrier for both CTAs' bytes and issues
+// every MMA; its commits release the stage in both CTAs and hand each CTA's accumulator (its
+// 128 TMEM lanes) to that CTA's epilogue.  No load uses multicast: each CTA fetches its own data.
+namespace pair {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 6;  // BM, BN: this CTA's rows / the tile's columns
+constexpr int TILE_M = 2 * BM;                           // rows per cluster tile
+constexpr int NUM_THREADS = 192;
+constexpr int A_STAGE_BYTES = BM * BK * 2;      // 16 KB
+constexpr int B_CHUNK_BYTES = BK * 64 * 2;      // 8 KB
+constexpr int B_STAGE_BYTES = BK * (BN / 2) * 2;  // 16 KB: this CTA's 128 columns
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 8;  // in 256-row blocks
+constexpr uint32_t IDESC = idesc_bf16_f32(TILE_M, BN, /*a_mn_major=*/0, /*b_mn_major=*/1);
+
+struct SharedTail {
+  uint64_t full[STAGES];       // used in the leader only: both CTAs' bytes for the stage landed
+  uint64_t empty[STAGES];      // per CTA: the leader's MMAs are done with this CTA's stage
+  uint64_t tmem_full[2];       // per CTA: its accumulator half is final
+  uint64_t tmem_empty[2];      // used in the leader only: 8 epilogue warps (both CTAs) drained it
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + sizeof(SharedTail);
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int group = GROUP_M * tiles_n;
+  const int g = t / group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(GROUP_M, tiles_m - first_m);
+  const int r = t - g * group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         __nv_bfloat16* __restrict__ C, int M, int N, int K, unsigned* err_word) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // Both CTAs compute the same aligned offsets (the MMA descriptors name one offset for both).
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * A_STAGE_BYTES;
+  SharedTail* st = reinterpret_cast<SharedTail*>(smem + STAGES * STAGE_BYTES);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = static_cast<int>(blockIdx.x) >> 1;
+  const int num_clusters = static_cast<int>(gridDim.x) >> 1;
+  const int tiles_m = (M + TILE_M - 1) / TILE_M;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&st->tmem_full[b], 1);
+      mbar_init(&st->tmem_empty[b], 8);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init_cluster();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barrier inits and the TMEM allocation visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        int mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        const int row0 = mb * TILE_M + static_cast<int>(rank) * BM;
+        const int col0 = nb * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          // empty[stage] (this CTA's) next completes for the use after this one, which needs the
+          // load issued here: the parity wait is unambiguous.
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&st->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&st->full[stage], 2 * STAGE_BYTES);
+          tma_load_2d_pair(smem_a + stage * A_STAGE_BYTES, &map_a, kb * BK, row0, full_leader);
+          uint8_t* bdst = smem_b + stage * B_STAGE_BYTES;
+#pragma unroll
+          for (int c = 0; c < BN / 128; ++c)
+            tma_load_2d_pair(bdst + c * B_CHUNK_BYTES, &map_b, col0 + c * 64, kb * BK, full_leader);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: the leader's last commits on this CTA's empty barriers (and so every MMA read of
+      // this CTA's stages) must land before the CTA may exit.  Bounded.
+      // Use u of a stage is released by phase u / STAGES of its empty barrier.
+      for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->empty[u % STAGES], (u / STAGES) & 1) && !*abort_flag &&
+               globaltimer_ns() - t0 < 200000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        // tmem_empty[acc] next completes after this accumulator is committed again (below).
+        if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          // full[stage] next completes for the stage's next use, whose loads wait on empty[stage],
+          // committed only below.
+          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * A_STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(smem_b + stage * B_STAGE_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t bdesc = smem_desc_sw128(b_addr + k * 2048, B_CHUNK_BYTES, 1024);
+            umma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            issued = true;
+          }
+          umma_commit_pair(&st->empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(&st->tmem_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_pair(&st->drain, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = (N % 8) == 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      int mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      // tmem_full[acc] next completes after this warp releases the accumulator (below).
+      if (!mbar_wait_bounded(&st->tmem_full[acc], acc_phase, abort_flag, err_word, kErrGemmEpilogueWait)) break;
+      tc_fence_after();
+      const int row = mb * TILE_M + static_cast<int>(rank) * BM + row_in_tile;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+      __nv_bfloat16* crow = C + static_cast<long long>(row) * N;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c0, r);
+        const int col = nb * BN + c0;
+        if (row < M && col < N) {
+          if (vec_ok && col + 32 <= N) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + col);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(r[q * 8 + 0]), __uint_as_float(r[q * 8 + 1]));
+              v.y = pack_bf16x2(__uint_as_float(r[q * 8 + 2]), __uint_as_float(r[q * 8 + 3]));
+              v.z = pack_bf16x2(__uint_as_float(r[q * 8 + 4]), __uint_as_float(r[q * 8 + 5]));
+              v.w = pack_bf16x2(__uint_as_float(r[q * 8 + 6]), __uint_as_float(r[q * 8 + 7]));
+              dst[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col + j < N) crow[col + j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&st->tmem_empty[acc]), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs, commits or loads can touch it
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace pair
+
 // ---- host side ------------------------------------------------------------------------------
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -319,12 +563,38 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bf
   return cudaGetLastError();
 }
 
+// 2-SM variant: clusters of two CTAs, 256x256 tiles.
+cudaError_t gemm_bf16_tc2(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                          cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  CUtensorMap ma, mb;
+  if (!make_tmap_bf16_2d(&ma, a, m, k, k, pair::BM, pair::BK)) return cudaErrorInvalidValue;
+  if (!make_tmap_bf16_2d(&mb, b, k, n, n, pair::BK, 64)) return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent attribute set
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(pair::gemm_bf16_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(pair::SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int tiles = ((m + pair::TILE_M - 1) / pair::TILE_M) * ((n + pair::BN - 1) / pair::BN);
+  const int clusters = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;
+  pair::gemm_bf16_tc2_kernel<<<2 * clusters, pair::NUM_THREADS, pair::SMEM_BYTES, s>>>(ma, mb, c, m, n, k,
+                                                                                       ctx->err_word);
+  return cudaGetLastError();
+}
+
 cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
                       cudaStream_t s) {
   std::string cfg;
-  const bool forced_simt = tune_lookup(LC_TUNE_MATMUL, m, k, n, 1 /*bf16*/, &cfg) && cfg == "simt";
-  if (!forced_simt && gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_tc(a, b, c, m, k, n, s);
-  return gemm_bf16_simt(a, b, c, m, k, n, s);
+  const bool tuned = tune_lookup(LC_TUNE_MATMUL, m, k, n, 1 /*bf16*/, &cfg);
+  if ((tuned && cfg == "simt") || !gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_simt(a, b, c, m, k, n, s);
+  if (tuned && cfg == kGemmTc2Name) return gemm_bf16_tc2(a, b, c, m, k, n, s);
+  if (tuned && cfg == kGemmTcName) return gemm_bf16_tc(a, b, c, m, k, n, s);
+  // Untuned: the 2-SM 256x256 tile once there are enough tiles to fill most of the SM pairs.
+  const bool big = m >= 256 && static_cast<long long>(m) * n >= 64LL * 256 * 256;
+  return big ? gemm_bf16_tc2(a, b, c, m, k, n, s) : gemm_bf16_tc(a, b, c, m, k, n, s);
 }
 
 }  // namespace lcb

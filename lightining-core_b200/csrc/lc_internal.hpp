@@ -37,8 +37,13 @@ cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloa
 cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
                            cudaStream_t s);
 bool gemm_bf16_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n);
+// The two tcgen05 kernels by their tune-cache names: 1-SM 128x256 tiles, 2-SM (cluster pair) 256x256.
+constexpr const char* kGemmTcName = "tcgen05_128x256";
+constexpr const char* kGemmTc2Name = "tcgen05_2sm_256x256";
 cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
                          cudaStream_t s);
+cudaError_t gemm_bf16_tc2(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                          cudaStream_t s);
 
 // ---- conv ---------------------------------------------------------------------------------
 // Implicit-GEMM NCHW conv, fp32 strict; bias may be null.  Output NCHW, so channel blocks of an

@@ -201,7 +201,10 @@ lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, si
   if (dtype == LC_DTYPE_F32) {
     for (int t = 0; t < simt_tile_count(); ++t) cands.push_back({simt_tile_name(t), t});
   } else {
-    if (gemm_bf16_tc_supported(a, b, out, (int)m, (int)k, (int)n)) cands.push_back({"tcgen05_128x256", -2});
+    if (gemm_bf16_tc_supported(a, b, out, (int)m, (int)k, (int)n)) {
+      cands.push_back({kGemmTcName, -2});
+      cands.push_back({kGemmTc2Name, -3});
+    }
     cands.push_back({"simt", -1});
   }
   auto run = [&](const Cand& c) -> cudaError_t {
@@ -211,8 +214,9 @@ lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, si
     const auto* A = static_cast<const __nv_bfloat16*>(a);
     const auto* B = static_cast<const __nv_bfloat16*>(b);
     auto* C = static_cast<__nv_bfloat16*>(out);
-    return c.tile == -2 ? gemm_bf16_tc(A, B, C, (int)m, (int)k, (int)n, s)
-                        : gemm_bf16_simt(A, B, C, (int)m, (int)k, (int)n, s);
+    if (c.tile == -2) return gemm_bf16_tc(A, B, C, (int)m, (int)k, (int)n, s);
+    if (c.tile == -3) return gemm_bf16_tc2(A, B, C, (int)m, (int)k, (int)n, s);
+    return gemm_bf16_simt(A, B, C, (int)m, (int)k, (int)n, s);
   };
   cudaEvent_t e0, e1;
   if (cudaEventCreate(&e0) != cudaSuccess) return LC_DRIVER_ERROR;

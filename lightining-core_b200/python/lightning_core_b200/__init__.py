@@ -441,6 +441,11 @@ def tune_cache_set(kind: int, d0: int, d1: int, d2: int, config: str, dtype: int
     check(lib.lcTuneCacheSet(kind, d0, d1, d2, dtype, config.encode()), "tune_cache_set")
 
 
+def tune_cache_reset(kind: int = TUNE_MATMUL) -> None:
+    """Drops every entry of one cache (the reference's matMulMetalResetTuning)."""
+    check(lib.lcTuneCacheReset(kind), "tune_cache_reset")
+
+
 def matmul_autotune(a: "DeviceBuffer", b: "DeviceBuffer", out: "DeviceBuffer", m: int, k: int, n: int,
                     dtype: int = F32) -> str:
     buf = C.create_string_buffer(64)

@@ -121,6 +121,24 @@ def test_matmul_bf16_shapes(gpu, m, k, n):
     close_enough(ref, out[rows], 2e-3, 2e-2)
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05_128x256", "tcgen05_2sm_256x256"])
+@pytest.mark.parametrize("m,k,n", [(256, 64, 256), (300, 72, 264), (2176, 520, 1288), (1000, 1000, 1000)])
+def test_matmul_bf16_each_tc_kernel(gpu, kernel, m, k, n):
+    """Both tcgen05 GEMMs (1-SM 128x256 and the 2-SM cluster-pair 256x256 tile), forced through the
+    tune cache, on shapes with M/N/K tails and fewer tiles than SM pairs."""
+    rng = np.random.default_rng(m + 3 * k + 5 * n)
+    a = P.bf16_round((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32))
+    b = P.bf16_round(rng.uniform(-1, 1, (k, n)).astype(np.float32))
+    gpu.tune_cache_set(gpu.TUNE_MATMUL, m, k, n, kernel, gpu.BF16)
+    try:
+        out = gpu.from_bf16(gpu.matmul2d(bf(gpu, a), bf(gpu, b), dtype=gpu.BF16))
+    finally:
+        gpu.tune_cache_reset()
+    rows = np.unique(np.linspace(0, m - 1, min(m, 96)).astype(int))
+    ref = P.matmul(np.ascontiguousarray(a[rows]), b, threads=8)
+    close_enough(ref, out[rows], 2e-3, 2e-2)
+
+
 # ---------------------------------------------------------------- conv + integrated pipeline
 @pytest.mark.parametrize("name,stride,pad,relu", [("parity_conv", (1, 1), (1, 1), False),
                                                   ("conv_stride2_pad0", (2, 1), (0, 1), True)])
