@@ -300,7 +300,7 @@ def run_ours(args, rank, world, local_rank):
         "frac_of_peak": value / peak, "peak_tflops": peak, "peak_kind": pk_kind,
         "parts": {"attention_ms": attn_avg, "attention_tflops": attn_ach, "attention_frac": attn_ach / peak,
                   "gemm_ms": gemm_avg, "gemm_tflops": gemm_ach, "gemm_frac": gemm_ach / peak},
-        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tc_kernel", "achieved": gemm_ach, "peak": peak,
+        "roofline": {"bound": "tensor", "kernel": "gemm_bf16_tc2_kernel", "achieved": gemm_ach, "peak": peak,
                      "unit": "TFLOP/s", "frac": gemm_ach / peak,
                      "peak_source": f"{pk_kind} bf16_tflops (burst; kernel timed alone)",
                      "traffic": None if traffic is None else traffic * nr / GM},
