@@ -253,6 +253,26 @@ lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, const float
                                      size_t stride_w, size_t pad_h, size_t pad_w, size_t seq, size_t head_dim,
                                      size_t proj_cols, int per_image, lcStream_t stream);
 
+/* Graph fused pattern attention_proj_v1 (GraphIR::executeAttentionProjFusedNodeTyped,
+ * include/lightning_core/core/graph.hpp:3454-3555): out[u] = attention(q[u], k[u], v[u]) @ proj_w,
+ * q/k/v [units, seq, head_dim], proj_w [head_dim, proj_cols], out [units, seq, proj_cols], scale
+ * 1/sqrt(head_dim); the graph passes causal = 0.  f32: one fused kernel (the projection runs in the
+ * attention epilogue) when head_dim, proj_cols <= 128, else attention then GEMM; bf16: tcgen05
+ * attention then tcgen05 GEMM.  Policy: upload_q/k/v as for attention, proj_w follows upload_q;
+ * the output postprocess fields must be neutral (scale 1, bias 0, no ReLU). */
+lcError_t lcAttentionProjForward(const void* q, const void* k, const void* v, const void* proj_w, void* out,
+                                 size_t units, size_t seq, size_t head_dim, size_t proj_cols, int causal,
+                                 lcDataType dtype, const lcAttentionIoPolicy* policy, lcStream_t stream);
+
+/* Graph fused pattern attention_qkv_proj_v1 (graph.hpp:3556-3584 with the kQkvPackRepeat node,
+ * graph.hpp:3138-3185): Q, K, V are the consecutive [seq, head_dim] flat slices of `packed`
+ * (packed_len floats, repeated cyclically when shorter than 3*seq*head_dim), then non-causal
+ * attention and the projection as above.  f32 only, like the reference's pack node.  `packed`
+ * follows upload_q, proj_w too. */
+lcError_t lcAttentionQkvProjForward(const float* packed, size_t packed_len, const float* proj_w, float* out,
+                                    size_t seq, size_t head_dim, size_t proj_cols,
+                                    const lcAttentionIoPolicy* policy, lcStream_t stream);
+
 /* out = a + b (f32 or f64); replaces vectorAddCuda (src/ops/vector_add_cuda.cu:12-86). */
 lcError_t lcVectorAdd(const void* a, const void* b, void* out, size_t n, lcDataType dtype,
                       const lcVectorAddIoPolicy* policy, lcStream_t stream);

@@ -187,6 +187,133 @@ lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* 
   return check_error_word(pol.synchronize || pol.download_out);
 }
 
+// Attention of `units` heads followed by the projection out[u] = attn[u] @ proj_w.  q/k/v of unit u
+// start u * unit_stride elements in; out is [units, seq, cols].  f32 with head_dim, cols <= 128
+// runs as one kernel (projection in the attention epilogue); otherwise attention into a scratch
+// buffer, then one GEMM over all units' rows.
+static lcError_t attention_proj_device(const void* dq, const void* dk, const void* dv, long long unit_stride,
+                                       const void* dp, void* dout, size_t units, size_t seq, size_t head_dim,
+                                       size_t cols, int causal, lcDataType dtype, Io& io) {
+  const size_t es = elem_size(dtype);
+  const bool fused = dtype == LC_DTYPE_F32 && head_dim <= 128 && cols <= 128;
+  void* attn = nullptr;
+  if (!fused) LC_TRY(io.scratch(units * seq * head_dim * es, &attn));
+  trace_op(kOpAttention, units * seq * seq * head_dim);
+  for (size_t u0 = 0; u0 < units; u0 += 65535) {
+    const size_t n = units - u0 < 65535 ? units - u0 : 65535;
+    AttnArgs a{};
+    a.q = static_cast<const char*>(dq) + u0 * unit_stride * es;
+    a.k = static_cast<const char*>(dk) + u0 * unit_stride * es;
+    a.v = static_cast<const char*>(dv) + u0 * unit_stride * es;
+    a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = unit_stride;
+    a.units = static_cast<int>(n);
+    a.seq = static_cast<int>(seq);
+    a.d = static_cast<int>(head_dim);
+    a.causal = causal ? 1 : 0;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.post_scale = 1.0f;
+    a.post_bias = 0.0f;
+    a.post_relu = 0;
+    if (fused) {
+      a.out = static_cast<char*>(dout) + u0 * seq * cols * es;
+      a.out_unit_stride = static_cast<long long>(seq * cols);
+      a.proj_w = static_cast<const float*>(dp);
+      a.proj_cols = static_cast<int>(cols);
+      LC_TRY(attention_f32(a, io.stream()));
+    } else {
+      a.out = static_cast<char*>(attn) + u0 * seq * head_dim * es;
+      a.out_unit_stride = static_cast<long long>(seq * head_dim);
+      LC_TRY(dtype == LC_DTYPE_F32 ? attention_f32(a, io.stream()) : attention_bf16(a, io.stream()));
+    }
+  }
+  if (!fused) {
+    const size_t rows = units * seq;
+    if (rows > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+    trace_op(kOpMatMul, rows * head_dim * cols);
+    LC_TRY(dtype == LC_DTYPE_F32
+               ? gemm_f32(static_cast<const float*>(attn), static_cast<const float*>(dp), static_cast<float*>(dout),
+                          (int)rows, (int)head_dim, (int)cols, io.stream())
+               : gemm_bf16(static_cast<const __nv_bfloat16*>(attn), static_cast<const __nv_bfloat16*>(dp),
+                           static_cast<__nv_bfloat16*>(dout), (int)rows, (int)head_dim, (int)cols, io.stream()));
+  }
+  return LC_SUCCESS;
+}
+
+static bool neutral_postprocess(const lcAttentionIoPolicy& p) {
+  return p.output_scale == 1.0f && p.output_bias == 0.0f && !p.output_relu;
+}
+
+lcError_t lcAttentionProjForward(const void* q, const void* k, const void* v, const void* proj_w, void* out,
+                                 size_t units, size_t seq, size_t head_dim, size_t proj_cols, int causal,
+                                 lcDataType dtype, const lcAttentionIoPolicy* policy, lcStream_t stream) {
+  if (!q || !k || !v || !proj_w || !out || units == 0 || seq == 0 || head_dim == 0 || proj_cols == 0)
+    return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_BF16) return LC_NOT_SUPPORTED;
+  if (seq > (size_t)INT_MAX || head_dim > 256 || units > (size_t)INT_MAX || proj_cols > (size_t)INT_MAX)
+    return LC_NOT_SUPPORTED;
+  lcAttentionIoPolicy pol;
+  if (policy) {
+    pol = *policy;
+  } else {
+    lcAttentionIoPolicyDefault(&pol);
+    pol.upload_q = pol.upload_k = pol.upload_v = pol.download_out = pol.synchronize = 0;
+  }
+  if (!neutral_postprocess(pol)) return LC_NOT_SUPPORTED;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t es = elem_size(dtype);
+  const size_t in_bytes = units * seq * head_dim * es, out_bytes = units * seq * proj_cols * es;
+  const void *dq, *dk, *dv, *dp;
+  void* dout;
+  LC_TRY(io.in(q, in_bytes, pol.upload_q, &dq));
+  LC_TRY(io.in(k, in_bytes, pol.upload_k, &dk));
+  LC_TRY(io.in(v, in_bytes, pol.upload_v, &dv));
+  LC_TRY(io.in(proj_w, head_dim * proj_cols * es, pol.upload_q, &dp));
+  LC_TRY(io.out(out, out_bytes, pol.download_out, &dout));
+  const lcError_t st = attention_proj_device(dq, dk, dv, static_cast<long long>(seq * head_dim), dp, dout, units, seq,
+                                             head_dim, proj_cols, causal, dtype, io);
+  if (st != LC_SUCCESS) return st;
+  LC_TRY(io.finish(out, dout, out_bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
+lcError_t lcAttentionQkvProjForward(const float* packed, size_t packed_len, const float* proj_w, float* out,
+                                    size_t seq, size_t head_dim, size_t proj_cols,
+                                    const lcAttentionIoPolicy* policy, lcStream_t stream) {
+  if (!packed || packed_len == 0 || !proj_w || !out || seq == 0 || head_dim == 0 || proj_cols == 0)
+    return LC_INVALID_VALUE;
+  if (seq > (size_t)INT_MAX || head_dim > 256 || proj_cols > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  lcAttentionIoPolicy pol;
+  if (policy) {
+    pol = *policy;
+  } else {
+    lcAttentionIoPolicyDefault(&pol);
+    pol.upload_q = pol.upload_k = pol.upload_v = pol.download_out = pol.synchronize = 0;
+  }
+  if (!neutral_postprocess(pol)) return LC_NOT_SUPPORTED;
+  Io io(static_cast<cudaStream_t>(stream));
+  const size_t need = seq * head_dim;
+  const size_t out_bytes = seq * proj_cols * 4;
+  const size_t used = packed_len < 3 * need ? packed_len : 3 * need;  // only the first 3*need floats matter
+  const void *dsrc, *dp;
+  void* dout;
+  LC_TRY(io.in(packed, used * 4, pol.upload_q, &dsrc));
+  LC_TRY(io.in(proj_w, head_dim * proj_cols * 4, pol.upload_q, &dp));
+  LC_TRY(io.out(out, out_bytes, pol.download_out, &dout));
+  const float* qkv = static_cast<const float*>(dsrc);
+  if (used < 3 * need) {
+    // The pack node repeats a short input cyclically up to 3*need floats (graph.hpp:3170-3180).
+    void* full;
+    LC_TRY(io.scratch(3 * need * 4, &full));
+    LC_TRY(repeat_fill_f32(qkv, used, static_cast<float*>(full), 3 * need, io.stream()));
+    qkv = static_cast<const float*>(full);
+  }
+  const lcError_t st = attention_proj_device(qkv, qkv + need, qkv + 2 * need, static_cast<long long>(3 * need), dp,
+                                             dout, 1, seq, head_dim, proj_cols, 0, LC_DTYPE_F32, io);
+  if (st != LC_SUCCESS) return st;
+  LC_TRY(io.finish(out, dout, out_bytes, pol.download_out, pol.synchronize));
+  return check_error_word(pol.synchronize || pol.download_out);
+}
+
 lcError_t lcMatMul(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
                    const lcMatMulIoPolicy* policy, lcStream_t stream) {
   if (!a || !b || !out || m == 0 || k == 0 || n == 0) return LC_INVALID_VALUE;

@@ -83,6 +83,8 @@ _SIGS = {
     "lcMatMul": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, C.POINTER(MatMulIoPolicy), _vp]),
     "lcConv2dNchw": (_i, [_vp, _vp, _vp, _vp] + [_sz] * 11 + [_i, C.POINTER(Conv2dIoPolicy), _vp]),
     "lcConvAttentionNchw": (_i, [_vp] * 5 + [_sz] * 14 + [_i, C.POINTER(Conv2dIoPolicy), _vp]),
+    "lcAttentionProjForward": (_i, [_vp] * 5 + [_sz] * 4 + [_i, _i, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcAttentionQkvProjForward": (_i, [_vp, _sz, _vp, _vp, _sz, _sz, _sz, C.POINTER(AttentionIoPolicy), _vp]),
     "lcVectorAdd": (_i, [_vp, _vp, _vp, _sz, _i, C.POINTER(VectorAddIoPolicy), _vp]),
     "lcLayerNorm": (_i, [_vp, _vp, _sz, _sz, _f, _vp]),
     "lcGetDeviceErrorWord": (_i, [C.POINTER(C.c_uint)]),
@@ -252,6 +254,42 @@ def attention_batched(q, k, v, causal: bool = False, dtype: int = F32):
     pol = default_attention_policy()
     check(lib.lcAttentionForward(_vp(q), _vp(np.ascontiguousarray(k)), _vp(np.ascontiguousarray(v)), _vp(out),
                                  units, s, d, int(causal), dtype, C.byref(pol), None), "attention")
+    return out
+
+
+def attention_proj(q, k, v, proj_w, causal: bool = False, dtype: int = F32):
+    """Graph fused node attention_proj_v1 (graph.hpp:3454-3555): attention(q, k, v) @ proj_w.
+
+    q, k, v: host [seq, d] or [units, seq, d]; proj_w [d, cols]; float32, or uint16 bf16 bits with
+    dtype=BF16.  Returns [.., seq, cols]."""
+    q = np.ascontiguousarray(q)
+    squeeze = q.ndim == 2
+    q3 = q[None] if squeeze else q
+    units, s, d = q3.shape
+    proj_w = np.ascontiguousarray(proj_w)
+    if proj_w.ndim != 2 or proj_w.shape[0] != d:
+        raise ValueError("proj_w must be [head_dim, cols]")
+    cols = proj_w.shape[1]
+    out = np.empty((units, s, cols), dtype=q.dtype)
+    pol = default_attention_policy()
+    check(lib.lcAttentionProjForward(_vp(q3), _vp(np.ascontiguousarray(k)), _vp(np.ascontiguousarray(v)),
+                                     _vp(proj_w), _vp(out), units, s, d, cols, int(causal), dtype, C.byref(pol),
+                                     None), "attention_proj")
+    return out[0] if squeeze else out
+
+
+def attention_qkv_proj(packed, proj_w, seq_len: int, head_dim: int):
+    """Graph fused node attention_qkv_proj_v1 (graph.hpp:3138-3185, 3556-3584): Q, K, V are the
+    consecutive [seq, d] slices of the flat `packed` float32 input (repeated cyclically when
+    short), then attention and the projection.  Returns [seq, cols] float32."""
+    packed = np.ascontiguousarray(packed, dtype=np.float32).reshape(-1)
+    proj_w = np.ascontiguousarray(proj_w, dtype=np.float32)
+    if proj_w.ndim != 2 or proj_w.shape[0] != head_dim:
+        raise ValueError("proj_w must be [head_dim, cols]")
+    out = np.empty((seq_len, proj_w.shape[1]), np.float32)
+    pol = default_attention_policy()
+    check(lib.lcAttentionQkvProjForward(_vp(packed), packed.size, _vp(proj_w), _vp(out), seq_len, head_dim,
+                                        proj_w.shape[1], C.byref(pol), None), "attention_qkv_proj")
     return out
 
 

@@ -174,6 +174,16 @@ class _Lib:
 _cache: dict = {}
 
 
+def qkv_pack_repeat(flat, need):
+    """The graph's kQkvPackRepeat node (reference include/lightning_core/core/graph.hpp:3138-3185):
+    the first 3*need floats of `flat`, repeated cyclically when shorter, split into Q, K, V."""
+    flat = np.asarray(flat, np.float32).reshape(-1)
+    total = 3 * need
+    reps = -(-total // flat.size)
+    packed = np.tile(flat, reps)[:total]
+    return packed[:need], packed[need:2 * need], packed[2 * need:]
+
+
 def port() -> _Lib:
     if "port" not in _cache:
         _cache["port"] = _Lib(PORT_SO, "orc")

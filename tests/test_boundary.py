@@ -92,6 +92,13 @@ def test_invalid_arguments_rejected_before_gpu(lc):
     assert L.lcVectorAdd(x, x, None, 4, lc.F32, None, None) == lc.LC_INVALID_VALUE
     assert L.lcVectorAdd(x, x, x, 4, lc.BF16, None, None) == lc.LC_NOT_SUPPORTED
     assert L.lcLayerNorm(x, x, 0, 4, 1e-5, None) == lc.LC_INVALID_VALUE
+    # graph fused nodes: missing projection / zero columns / non-neutral postprocess
+    assert L.lcAttentionProjForward(x, x, x, None, x, 1, 4, 4, 4, 0, lc.F32, None, None) == lc.LC_INVALID_VALUE
+    assert L.lcAttentionProjForward(x, x, x, x, x, 1, 4, 4, 0, 0, lc.F32, None, None) == lc.LC_INVALID_VALUE
+    pol = lc.default_attention_policy()
+    pol.output_relu = 1
+    assert L.lcAttentionProjForward(x, x, x, x, x, 1, 4, 4, 4, 0, lc.F32, C.byref(pol), None) == lc.LC_NOT_SUPPORTED
+    assert L.lcAttentionQkvProjForward(x, 0, x, x, 4, 4, 4, None, None) == lc.LC_INVALID_VALUE
 
 
 def test_policy_defaults_and_loop_presets(lc):

@@ -139,6 +139,47 @@ def test_matmul_bf16_each_tc_kernel(gpu, kernel, m, k, n):
     close_enough(ref, out[rows], 2e-3, 2e-2)
 
 
+# ---------------------------------------------------------------- graph fused nodes
+@pytest.mark.parametrize("units,seq,d,cols,causal", [(1, 256, 64, 64, 0), (3, 100, 64, 48, 0), (2, 130, 64, 160, 1),
+                                                     (1, 77, 32, 8, 0)])
+def test_attention_proj_f32(gpu, units, seq, d, cols, causal):
+    """attention_proj_v1: attention then @ proj_w, fused in one kernel for d, cols <= 128 and
+    attention + GEMM otherwise (cols = 160)."""
+    rng = np.random.default_rng(units * 1000 + seq + cols)
+    q, k, v = (rng.standard_normal((units, seq, d)).astype(np.float32) for _ in range(3))
+    w = (rng.uniform(-1, 1, (d, cols)) * np.sqrt(6.0 / d)).astype(np.float32)
+    out = gpu.attention_proj(q, k, v, w, causal=bool(causal))
+    for u in range(units):
+        ref = P.matmul(P.attention(q[u], k[u], v[u], causal=bool(causal)), w)
+        close_enough(ref, out[u], *F32_TOL)
+
+
+def test_attention_proj_bf16(gpu):
+    rng = np.random.default_rng(21)
+    units, seq, d, cols = 4, 384, 128, 128
+    q, k, v = (P.bf16_round(rng.standard_normal((units, seq, d)).astype(np.float32)) for _ in range(3))
+    w = P.bf16_round((rng.uniform(-1, 1, (d, cols)) / np.sqrt(d)).astype(np.float32))
+    out = gpu.from_bf16(gpu.attention_proj(bf(gpu, q), bf(gpu, k), bf(gpu, v), bf(gpu, w), causal=True,
+                                           dtype=gpu.BF16))
+    for u in range(units):
+        attn = P.bf16_round(P.attention(q[u], k[u], v[u], causal=True))
+        close_enough(P.matmul(attn, w), out[u], 2e-2, 3e-2)
+
+
+@pytest.mark.parametrize("have_factor", [3.0, 1.4, 0.3])
+def test_attention_qkv_proj(gpu, have_factor):
+    """attention_qkv_proj_v1 with a packed input of 3x, 1.4x and 0.3x seq*d floats (the short
+    ones take the pack node's cyclic repeat)."""
+    seq, d, cols = 196, 64, 64
+    rng = np.random.default_rng(int(have_factor * 10))
+    flat = rng.standard_normal(int(have_factor * seq * d)).astype(np.float32)
+    w = (rng.uniform(-1, 1, (d, cols)) * np.sqrt(6.0 / d)).astype(np.float32)
+    out = gpu.attention_qkv_proj(flat, w, seq, d)
+    q, k, v = (x.reshape(seq, d) for x in O.qkv_pack_repeat(flat, seq * d))
+    ref = P.matmul(P.attention(q, k, v, causal=False), w)
+    close_enough(ref, out, *F32_TOL)
+
+
 # ---------------------------------------------------------------- conv + integrated pipeline
 @pytest.mark.parametrize("name,stride,pad,relu", [("parity_conv", (1, 1), (1, 1), False),
                                                   ("conv_stride2_pad0", (2, 1), (0, 1), True)])

@@ -125,3 +125,21 @@ def test_matrix_ops_golden(P):
     np.testing.assert_array_equal(P.matrix_op("sub", g["a"], g["b"]), g["sub"])
     # the reference build (-ffast-math) divides approximately; its own parity tolerance is 2e-4
     close_enough(g["div"], P.matrix_op("div", g["a"], g["b"]), 2e-4, 2e-4)
+
+
+def test_qkv_pack_repeat_matches_reference_loop():
+    """oracle.qkv_pack_repeat against a literal restatement of the pack node's doubling copy
+    (reference include/lightning_core/core/graph.hpp:3168-3185)."""
+    rng = np.random.default_rng(11)
+    for have, need in [(5, 4), (12, 4), (100, 7), (3, 50), (600, 100)]:
+        flat = rng.standard_normal(have).astype(np.float32)
+        total = 3 * need
+        packed = np.zeros(total, np.float32)
+        copied = min(have, total)
+        packed[:copied] = flat[:copied]
+        while copied < total:
+            chunk = min(copied, total - copied)
+            packed[copied:copied + chunk] = packed[:chunk]
+            copied += chunk
+        q, k, v = O.qkv_pack_repeat(flat, need)
+        assert np.array_equal(np.concatenate([q, k, v]), packed)
