@@ -278,8 +278,15 @@ def run_ours(args, rank, world, local_rank):
     # ---- e2e through the C ABI with host buffers and the reference's default policy
     e2e = e2e_run(args, lc, torch, q, k, v, A, Bm, nu, nr, world, dev)
 
-    # ---- extra configs (N=1 only): fp32 attention [256,64], fp32 matmul 1024^3, conv->attention pipeline
-    extras = extra_configs(args, lc, torch, dev, sp) if world == 1 else None
+    # ---- extra configs: at N=1 the fp32 configs 1, 2, 5 and the HBM-bound ops; at N>1 config 5
+    # sharded by image (its natural shard unit), the others being replicas-only sizes.
+    if world == 1:
+        extras = extra_configs(args, lc, torch, dev, sp)
+    else:
+        try:
+            extras = sharded_cfg5(lc, torch, dev, sp, rank, world)
+        except Exception as exc:  # reported, never allowed to cost the headline line
+            extras = {"cfg5_conv_attention_f32_sharded": {"error": f"{type(exc).__name__}: {exc}"}}
 
     if rank != 0:
         return
@@ -352,6 +359,57 @@ def e2e_run(args, lc, torch, q, k, v, A, Bm, nu, nr, world, dev):
     return {"value": total_flops / dt / 1e12, "unit": "TFLOP/s", "ms_per_step": dt * 1e3,
             "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
             "timing": "wall clock around synchronous C-ABI calls, max over ranks", "steps": steps}
+
+
+def sharded_cfg5(lc, torch, dev, sp, rank, world):
+    """Config 5 (conv [32,64,56,56] -> QKV -> attention -> projection, fp32) with the 32 images split
+    across ranks: compute time = max over ranks (CUDA events), then the NCCL all-gather that
+    assembles [32, 3136, 64] on every rank, timed separately."""
+    import torch.distributed as dist
+    from lightning_core_b200.sharding import assemble, shard_range
+
+    L = lc.lib
+    ptr = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    stream = torch.cuda.current_stream()
+    images = 32
+    i0, i1 = shard_range(images, rank, world)
+    n = i1 - i0
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    x = torch.randn((images, 64, 56, 56), generator=g, device=dev)[i0:i1].contiguous()
+    bound = (6 / 576) ** 0.5
+    w = (torch.rand((192, 64, 3, 3), generator=g, device=dev) * 2 - 1) * bound
+    bias = torch.zeros(192, device=dev)
+    g.manual_seed(5)
+    pw = (torch.rand((64, 64), generator=g, device=dev) * 2 - 1) * (6 / 64) ** 0.5
+    out = torch.empty((max(n, 1), 3136, 64), device=dev)
+
+    def run():
+        if n > 0:
+            lc.check(L.lcConvAttentionNchw(ptr(x), ptr(w), ptr(bias), ptr(pw), ptr(out), n, 64, 56, 56, 192, 3, 3, 1,
+                                           1, 1, 1, 3136, 64, 64, 1, None, sp))
+
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = 5
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    e0.record(stream)
+    for _ in range(reps):
+        run()
+    e1.record(stream)
+    full = assemble(out[:n], images, rank, world)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps, e1.elapsed_time(e2)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, asm_ms = (float(v) for v in t.tolist())
+    del full
+    flops = 2 * 32 * 3136 * 192 * 576 + 32 * 4 * 3136 ** 2 * 64 + 2 * 32 * 3136 * 64 * 64
+    return {"cfg5_conv_attention_f32_sharded": {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12,
+                                                "assemble_ms": asm_ms, "images_per_rank": f"{images}/{world}",
+                                                "timing": "CUDA events, max over ranks; all-gather timed apart"}}
 
 
 def extra_configs(args, lc, torch, dev, sp):
