@@ -1,0 +1,421 @@
+// Strict-fp32 GEMM on the 5th-generation tensor cores by the 3xTF32 split:
+//   a = a_hi + a_lo with a_hi = a rounded to tf32 and a_lo = a - a_hi (exact in fp32), likewise b,
+//   C = a_hi b_hi + a_hi b_lo + a_lo b_hi  (the dropped a_lo b_lo term is ~2^-22 |a b|),
+// accumulated in fp32 in TMEM.  Products and sums keep fp32-level accuracy, inside the 1e-4
+// contract of the reference's fp32 matMul (src/ops/matmul_cpu.cpp:49-60, ops.hpp:354-459), at
+// tensor-core rates.
+//
+// A pre-pass splits A [M,K] (row-major, as the reference) into hi/lo planes and B [K,N] into
+// hi/lo planes of B^T [N,K], so both operands are K-major in shared memory.  The GEMM is
+// persistent, one CTA per SM, 192 threads: warp 0 TMA (A planes 128x32, B^T planes 128x32,
+// 128-byte swizzle, 3-stage ring of 64 KB), warp 1 one thread issuing tcgen05.mma.kind::tf32
+// (M=128, N=128, K=8) three times per K step, warps 2..5 the epilogue.
+// Accuracy: the tensor core's fp32 accumulation over thousands of terms drifts by up to ~1e-3
+// (it does not round like a sequential fp32 sum), so the MMAs only accumulate 128-deep K chunks,
+// each into one of four rotating 128-column TMEM buffers, and the epilogue warps add the chunks
+// into per-row fp32 registers with round-to-nearest adds (one row of 128 columns per thread).
+// Every mbarrier wait is bounded (common.cuh).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/lc_b200.h"
+#include "common.cuh"
+#include "lc_internal.hpp"
+
+namespace lcb {
+
+void* tensor_map_encoder();
+
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int CHUNK_KB = 4;   // k-blocks (of 32) per TMEM partial sum: 128-deep K chunks
+constexpr int ACC_BUFS = 4;   // TMEM partial-sum buffers of BN columns
+constexpr int NUM_THREADS = 192;
+constexpr int A_PLANE_BYTES = BM * BK * 4;        // 16 KB
+constexpr int B_PLANE_BYTES = BN * BK * 4;        // 16 KB: 128 B^T rows x 32 K
+constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * B_PLANE_BYTES;  // hi + lo of each
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+constexpr uint32_t IDESC = idesc_tf32_f32(BM, BN, /*a_mn_major=*/0, /*b_mn_major=*/0);
+
+struct Tail {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tmem_full[ACC_BUFS];   // a K chunk's partial sum is in TMEM buffer b
+  uint64_t tmem_empty[ACC_BUFS];  // the 4 epilogue warps have folded buffer b into registers
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + sizeof(Tail);
+
+// x rounded to the 10-bit tf32 mantissa (nearest, ties away from zero), kept in fp32 layout with the
+// 13 low mantissa bits clear: add half a tf32 unit (bit 12) to the magnitude, then truncate.
+// Infinities and NaNs pass through.
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+  return __uint_as_float(u);
+}
+
+// B [K,N] -> hi/lo planes of B^T [N,K]: 32x32 tiles through shared memory (coalesced both ways).
+__global__ void tf32_split_transpose_kernel(const float* __restrict__ b, float* __restrict__ hi_t,
+                                            float* __restrict__ lo_t, int K, int N) {
+  __shared__ float tile[32][33];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int k = k0 + r, n = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (k < K && n < N) ? b[static_cast<size_t>(k) * N + n] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int n = n0 + r, k = k0 + threadIdx.x;
+    if (n < N && k < K) {
+      const float v = tile[threadIdx.x][r];
+      const float h = tf32_round(v);
+      hi_t[static_cast<size_t>(n) * K + k] = h;
+      lo_t[static_cast<size_t>(n) * K + k] = v - h;
+    }
+  }
+}
+
+// hi = tf32(x), lo = x - hi, four elements per thread.
+__global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
+                                  size_t n4) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 v = x[i];
+    float4 h, l;
+    h.x = tf32_round(v.x);
+    h.y = tf32_round(v.y);
+    h.z = tf32_round(v.z);
+    h.w = tf32_round(v.w);
+    l.x = v.x - h.x;
+    l.y = v.y - h.y;
+    l.z = v.z - h.z;
+    l.w = v.w - h.w;
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// Warp-uniform bounded wait (lane 0 polls, the verdict is broadcast) so the warp stays converged
+// for the .sync.aligned TMEM loads that follow.
+__device__ __forceinline__ bool warp_wait_gemm(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned* err) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, err, kErrGemmEpilogueWait) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int group = GROUP_M * tiles_n;
+  const int g = t / group;
+  const int first_m = g * GROUP_M;
+  const int gm = min(GROUP_M, tiles_m - first_m);
+  const int r = t - g * group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                       const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+                       float* __restrict__ C, int M, int N, int K, unsigned* err_word) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // Stage layout: A_hi | A_lo | B_hi | B_lo.
+  Tail* st = reinterpret_cast<Tail*>(smem + STAGES * STAGE_BYTES);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (M + BM - 1) / BM;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int b = 0; b < ACC_BUFS; ++b) {
+      mbar_init(&st->tmem_full[b], 1);
+      mbar_init(&st->tmem_empty[b], 4);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_ahi);
+    tma_prefetch_desc(&map_alo);
+    tma_prefetch_desc(&map_bhi);
+    tma_prefetch_desc(&map_blo);
+  }
+  if (warp == 0) {
+    tmem_alloc(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        int mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          // empty[stage] next completes for this stage's next use, which needs the loads below.
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          uint8_t* base = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&st->full[stage], STAGE_BYTES);
+          tma_load_2d(base, &map_ahi, kb * BK, mb * BM, &st->full[stage]);
+          tma_load_2d(base + A_PLANE_BYTES, &map_alo, kb * BK, mb * BM, &st->full[stage]);
+          tma_load_2d(base + 2 * A_PLANE_BYTES, &map_bhi, kb * BK, nb * BN, &st->full[stage]);
+          tma_load_2d(base + 2 * A_PLANE_BYTES + B_PLANE_BYTES, &map_blo, kb * BK, nb * BN, &st->full[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let the copies already issued land before the CTA's shared memory goes away.
+        for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&st->full[u % STAGES], (u / STAGES) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        uint32_t d_tmem = tmem_base;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int kc = kb % CHUNK_KB;
+          if (kc == 0) {
+            // Buffer acc was last committed ACC_BUFS chunks ago; tmem_empty[acc] next completes
+            // only after the commit that follows this wait.
+            if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+          }
+          // full[stage] next completes for the stage's next use, loaded only after the commit below.
+          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t a_lo = a_hi + A_PLANE_BYTES;
+          const uint32_t b_hi = a_hi + 2 * A_PLANE_BYTES;
+          const uint32_t b_lo = b_hi + B_PLANE_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            // A and B^T: K-major SW128, rows 128 B apart, 8-row groups 1 KB apart; +32 B per K=8 step.
+            const uint64_t ahd = smem_desc_sw128(a_hi + k * 32, 16, 1024);
+            const uint64_t ald = smem_desc_sw128(a_lo + k * 32, 16, 1024);
+            const uint64_t bhd = smem_desc_sw128(b_hi + k * 32, 16, 1024);
+            const uint64_t bld = smem_desc_sw128(b_lo + k * 32, 16, 1024);
+            const uint32_t first = (kc > 0 || k > 0) ? 1u : 0u;
+            umma_tf32_ss(d_tmem, ald, bhd, IDESC, first);  // small terms first
+            umma_tf32_ss(d_tmem, ahd, bld, IDESC, 1u);
+            umma_tf32_ss(d_tmem, ahd, bhd, IDESC, 1u);
+            issued = true;
+          }
+          umma_commit(&st->empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (kc == CHUNK_KB - 1 || kb == num_kb - 1) {
+            umma_commit(&st->tmem_full[acc]);
+            if (++acc == ACC_BUFS) {
+              acc = 0;
+              acc_phase ^= 1u;
+            }
+          }
+        }
+      }
+      if (!ok && issued) {
+        umma_commit(&st->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5): chunk sums -> fp32 rows ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = (N % 4) == 0;
+    const int chunks = (num_kb + CHUNK_KB - 1) / CHUNK_KB;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      float sum[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+      for (int ch = 0; ch < chunks; ++ch) {
+        // tmem_full[acc] next completes after this warp releases the buffer (below).
+        if (!warp_wait_gemm(&st->tmem_full[acc], acc_phase, abort_flag, err_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c0, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[c0 + j] = __fadd_rn(sum[c0 + j], __uint_as_float(r[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st->tmem_empty[acc]);
+        if (++acc == ACC_BUFS) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      const int row = mb * BM + row_in_tile;
+      if (row < M) {
+        float* crow = C + static_cast<long long>(row) * N + nb * BN;
+        const int left = N - nb * BN;
+        if (vec_ok && left >= BN) {
+#pragma unroll
+          for (int q = 0; q < BN / 4; ++q)
+            reinterpret_cast<float4*>(crow)[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN; ++j)
+            if (j < left) crow[j] = sum[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D fp32 tensor map over row-major [rows, cols], box [box_rows, box_cols], 128-byte swizzle.
+bool make_tmap_f32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                      uint32_t box_cols) {
+  auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t split(const float* x, float* hi, float* lo, size_t n, cudaStream_t s) {
+  const size_t n4 = n / 4;  // callers keep n a multiple of 4
+  const int blocks = static_cast<int>(n4 / 256 + 1 < 148 * 8 ? n4 / 256 + 1 : 148 * 8);
+  tf32_split_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(hi),
+                                            reinterpret_cast<float4*>(lo), n4);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool gemm_f32_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  return m > 0 && k > 0 && n > 0 && (k % 4) == 0 && (n % 4) == 0 && al(a) && al(b) && al(c) &&
+         tensor_map_encoder() != nullptr;
+}
+
+cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
+  const size_t bytes = 2 * (na + nb) * sizeof(float);
+  // The split planes live in a grow-only per-device workspace; `tf32_done` orders every launch
+  // that uses it after the previous one, whatever its stream.
+  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
+  cudaError_t e = cudaSuccess;
+  if (!ctx->tf32_done) e = cudaEventCreateWithFlags(&ctx->tf32_done, cudaEventDisableTiming);
+  if (e != cudaSuccess) return e;
+  if (ctx->tf32_ws_bytes < bytes) {
+    if (ctx->tf32_ws) {
+      e = cudaEventSynchronize(ctx->tf32_done);
+      if (e != cudaSuccess) return e;
+      cudaFree(ctx->tf32_ws);
+      ctx->tf32_ws = nullptr;
+      ctx->tf32_ws_bytes = 0;
+    }
+    e = cudaMalloc(reinterpret_cast<void**>(&ctx->tf32_ws), bytes);
+    if (e != cudaSuccess) return e;
+    ctx->tf32_ws_bytes = bytes;
+  }
+  float* a_hi = ctx->tf32_ws;
+  float* a_lo = a_hi + na;
+  float* b_hi = a_lo + na;
+  float* b_lo = b_hi + nb;
+  CUtensorMap mah, mal, mbh, mbl;
+  if (!make_tmap_f32_2d(&mah, a_hi, m, k, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, k, BM, BK) ||
+      !make_tmap_f32_2d(&mbh, b_hi, n, k, BN, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, k, BN, BK))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent attribute set
+  if (!attr_set) {
+    e = cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  e = cudaStreamWaitEvent(s, ctx->tf32_done, 0);
+  if (e == cudaSuccess) e = split(a, a_hi, a_lo, na, s);
+  if (e == cudaSuccess) {
+    tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return e;
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mah, mal, mbh, mbl, c, m, n, k, ctx->err_word);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventRecord(ctx->tf32_done, s);
+  return e;
+}
+
+}  // namespace lcb

@@ -6,6 +6,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <string>
 
 namespace lcb {
@@ -15,6 +16,11 @@ struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
   unsigned* err_word = nullptr;  // device word written by kernels whose bounded waits gave up
+  // Split planes of the 3xTF32 GEMM (grow-only); `tf32_done` orders the launches that use them.
+  std::mutex tf32_mu;
+  float* tf32_ws = nullptr;
+  size_t tf32_ws_bytes = 0;
+  cudaEvent_t tf32_done = nullptr;
 };
 DeviceCtx* device_ctx();
 
@@ -30,6 +36,11 @@ const char* simt_tile_name(int tile);
 int simt_tile_from_name(const char* name);
 // Tuned dispatch: consults the matmul auto-tune cache for (m, k, n, dtype).
 cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s);
+// Strict fp32 on tcgen05 by the 3xTF32 split (gemm_tf32x3.cu): k % 4 == 0, n % 4 == 0, 16-byte
+// aligned pointers.
+bool gemm_f32_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n);
+cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s);
+constexpr const char* kGemmTf32x3Name = "tcgen05_3xtf32";
 // bf16 in, fp32 accumulate, bf16 out.  tcgen05/TMA kernel when k%8==0 && n%8==0 and the
 // pointers are 16-byte aligned; otherwise a SIMT kernel with the same arithmetic contract.
 cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,

@@ -123,9 +123,16 @@ void tune_store(int kind, size_t d0, size_t d1, size_t d2, int dtype, const std:
 
 cudaError_t gemm_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
   std::string cfg;
-  int tile = -1;
-  if (tune_lookup(LC_TUNE_MATMUL, m, k, n, LC_DTYPE_F32, &cfg)) tile = simt_tile_from_name(cfg.c_str());
-  return gemm_f32_tile(a, b, c, m, k, n, tile, s);
+  const bool tc_ok = gemm_f32_tc_supported(a, b, c, m, k, n);
+  if (tune_lookup(LC_TUNE_MATMUL, m, k, n, LC_DTYPE_F32, &cfg)) {
+    if (cfg == kGemmTf32x3Name && tc_ok) return gemm_f32_3xtf32(a, b, c, m, k, n, s);
+    return gemm_f32_tile(a, b, c, m, k, n, simt_tile_from_name(cfg.c_str()), s);
+  }
+  // Untuned: the 3xTF32 tensor-core path once there is enough work to cover its pre-pass and
+  // launches (measured: 512x64x512 is faster on the SIMT kernel, 1000x516x1004 2x faster here).
+  if (tc_ok && m >= 256 && n >= 256 && static_cast<long long>(m) * n * k >= (1LL << 26))
+    return gemm_f32_3xtf32(a, b, c, m, k, n, s);
+  return gemm_f32_tile(a, b, c, m, k, n, -1, s);
 }
 
 }  // namespace lcb
@@ -200,6 +207,7 @@ lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, si
   std::vector<Cand> cands;
   if (dtype == LC_DTYPE_F32) {
     for (int t = 0; t < simt_tile_count(); ++t) cands.push_back({simt_tile_name(t), t});
+    if (gemm_f32_tc_supported(a, b, out, (int)m, (int)k, (int)n)) cands.push_back({kGemmTf32x3Name, -4});
   } else {
     if (gemm_bf16_tc_supported(a, b, out, (int)m, (int)k, (int)n)) {
       cands.push_back({kGemmTcName, -2});
@@ -208,6 +216,9 @@ lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, si
     cands.push_back({"simt", -1});
   }
   auto run = [&](const Cand& c) -> cudaError_t {
+    if (dtype == LC_DTYPE_F32 && c.tile == -4)
+      return gemm_f32_3xtf32(static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(out),
+                             (int)m, (int)k, (int)n, s);
     if (dtype == LC_DTYPE_F32)
       return gemm_f32_tile(static_cast<const float*>(a), static_cast<const float*>(b), static_cast<float*>(out),
                            (int)m, (int)k, (int)n, c.tile, s);

@@ -102,6 +102,23 @@ def test_matmul_f32_shapes(gpu, m, k, n):
     close_enough(P.matmul(a, b, threads=8), gpu.matmul2d(a, b), *F32_TOL)
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05_3xtf32", "simt128x128"])
+@pytest.mark.parametrize("m,k,n", [(1024, 1024, 1024), (300, 516, 260), (1000, 36, 1004), (129, 4100, 388)])
+def test_matmul_f32_each_kernel(gpu, kernel, m, k, n):
+    """Strict fp32 matmul on the 3xTF32 tensor-core kernel and on the SIMT kernel, forced through
+    the tune cache, within the 1e-4 contract of the reference CPU loop (tails in M, N and K)."""
+    rng = np.random.default_rng(m + 7 * k + 11 * n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    gpu.tune_cache_set(gpu.TUNE_MATMUL, m, k, n, kernel, gpu.F32)
+    try:
+        out = gpu.matmul2d(a, b)
+    finally:
+        gpu.tune_cache_reset()
+    rows = np.unique(np.linspace(0, m - 1, min(m, 64)).astype(int))
+    close_enough(P.matmul(np.ascontiguousarray(a[rows]), b, threads=8), out[rows], *F32_TOL)
+
+
 # ---------------------------------------------------------------- matmul bf16
 def test_matmul_bf16_golden(gpu):
     g = golden("cfg4_gemm_bf16in_192x256x264")
