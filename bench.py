@@ -218,8 +218,18 @@ def run_ours(args, rank, world, local_rank):
         lc.check(L.lcMatMul(C.c_void_p(A.data_ptr()), C.c_void_p(Bm.data_ptr()), C.c_void_p(Cm.data_ptr()), nr, GK,
                             GN, lc.BF16, None, sp), "matmul")
 
+    def f32gemm_fn():
+        # Strict fp32 matmul 2048^3 (config 2 family) through the default dispatch (3xTF32).
+        n = 2048
+        g.manual_seed(1)
+        fa = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        fb = torch.rand((n, n), generator=g, device=dev) * 2 - 1
+        fc = torch.empty_like(fa)
+        return lambda: lc.check(L.lcMatMul(C.c_void_p(fa.data_ptr()), C.c_void_p(fb.data_ptr()),
+                                           C.c_void_p(fc.data_ptr()), n, n, n, lc.F32, None, sp), "matmul f32")
+
     if args.only:
-        fn = {"gemm": gemm, "attention": attn}[args.only]
+        fn = {"gemm": gemm, "attention": attn, "f32gemm": None}[args.only] or f32gemm_fn()
         for _ in range(args.warmup + args.steps):
             fn()
         torch.cuda.synchronize()
@@ -484,7 +494,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["gemm", "attention"],
+    ap.add_argument("--only", default=None, choices=["gemm", "attention", "f32gemm"],
                     help="run only this kernel's warm-up + timed launches (for ncu captures); prints no JSON")
     args = ap.parse_args()
     # Libraries (NCCL's version banner, ...) may write to fd 1; keep it for the one JSON line only.
