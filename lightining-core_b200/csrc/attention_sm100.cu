@@ -4,9 +4,9 @@
 // batched bf16 config.  Output row i = sum_j softmax_j(q_i . k_j / sqrt(d)) v_j, j <= i if causal,
 // then the optional postprocess out*scale + bias (ReLU) of src/attention.cpp:41-60.
 //
-// One CTA = one 128-row Q tile of one (batch, head) unit; 192 threads:
+// One CTA = one 128-row Q tile of one (batch, head) unit, two CTAs per SM; 224 threads:
 //   warp 0      TMA: Q once, then K_j tiles (64 keys) into a 2-stage ring freed as soon as S_j
-//               is done; warp 6 loads V_j into its own buffer freed by PV_j (a separate thread,
+//               is done; warp 6 loads V_j into a 2-stage ring freed by PV_j (a separate thread,
 //               so a late V slot never holds back K); L2 prefetch of upcoming tiles; 3-D tensor
 //               maps [units, S, D] so rows past S read as zero; 128-byte swizzle.
 //   warp 1      MMA (one thread): S_j = Q K_j^T into one of two TMEM score buffers (so S_{j+1}
