@@ -80,12 +80,110 @@ class Io {
     return e;
   }
   cudaStream_t stream() const { return s_; }
+  int device() const { return dev_; }
 
  private:
   cudaStream_t s_;
   int dev_ = 0;
   int slot_ = 0;
 };
+
+// ---- pipelined staging ----------------------------------------------------------------------
+// A large call with host inputs and a host output is cut into chunks along its independent
+// dimension (attention units, GEMM rows): chunk c's uploads run on a helper stream, its kernel on
+// the caller's stream, its download on a second helper stream, so copies in both PCIe directions
+// overlap each other and the kernels.  Same results, same policy contract (the call returns with
+// the output in host memory).  Helper streams and events are per thread and device.
+struct PipeRes {
+  cudaStream_t in[64] = {}, out[64] = {};
+  std::vector<cudaEvent_t> ev[64];
+  cudaError_t streams(int dev, cudaStream_t* i, cudaStream_t* o) {
+    if (!in[dev]) {
+      cudaError_t e = cudaStreamCreateWithFlags(&in[dev], cudaStreamNonBlocking);
+      if (e != cudaSuccess) return e;
+      e = cudaStreamCreateWithFlags(&out[dev], cudaStreamNonBlocking);
+      if (e != cudaSuccess) return e;
+    }
+    *i = in[dev];
+    *o = out[dev];
+    return cudaSuccess;
+  }
+  cudaError_t event(int dev, size_t idx, cudaEvent_t* e) {
+    auto& v = ev[dev];
+    while (v.size() <= idx) {
+      cudaEvent_t x;
+      cudaError_t r = cudaEventCreateWithFlags(&x, cudaEventDisableTiming);
+      if (r != cudaSuccess) return r;
+      v.push_back(x);
+    }
+    *e = v[idx];
+    return cudaSuccess;
+  }
+};
+thread_local PipeRes t_pipe;
+constexpr size_t kPipeMinBytes = size_t(24) << 20;  // smaller calls gain nothing from chunking
+
+// One chunked host<->device transfer: element u of the chunked dimension is unit_bytes long.
+struct PipeBuf {
+  const void* host_in;   // host source (nullptr: device-resident, nothing to upload)
+  void* host_out;        // host destination (outputs)
+  void* dev;
+  size_t unit_bytes;
+};
+
+// Runs launch(u0, n) for n-unit chunks of [0, units) with `ins` uploaded and `out_buf`
+// downloaded chunk by chunk; `prefix` inputs are uploaded whole before the first chunk.  Chunks
+// are multiples of `align` units.  Returns with everything complete on the caller's stream
+// (the caller synchronizes).
+template <class Launch>
+cudaError_t run_pipelined(Io& io, size_t units, size_t align, const std::vector<PipeBuf>& prefix,
+                          const std::vector<PipeBuf>& ins, const PipeBuf& out_buf, Launch launch) {
+  const int dev = io.device();
+  cudaStream_t s = io.stream(), si, so;
+  cudaError_t e = t_pipe.streams(dev, &si, &so);
+  if (e != cudaSuccess) return e;
+  size_t per_unit = out_buf.unit_bytes;
+  for (const auto& b : ins) per_unit += b.host_in ? b.unit_bytes : 0;
+  const size_t total = per_unit * units;
+  size_t nchunks = total / (size_t(16) << 20);
+  nchunks = nchunks < 2 ? 2 : nchunks > 8 ? 8 : nchunks;
+  size_t chunk = (units + nchunks - 1) / nchunks;
+  chunk = (chunk + align - 1) / align * align;
+  cudaEvent_t start;
+  if ((e = t_pipe.event(dev, 0, &start)) != cudaSuccess) return e;
+  // Prior work on the caller's stream (e.g. kernels still reading the staging buffers) first.
+  if ((e = cudaEventRecord(start, s)) != cudaSuccess || (e = cudaStreamWaitEvent(si, start, 0)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(so, start, 0)) != cudaSuccess)
+    return e;
+  for (const auto& b : prefix)
+    if (b.host_in && (e = cudaMemcpyAsync(b.dev, b.host_in, b.unit_bytes, cudaMemcpyHostToDevice, si)) != cudaSuccess)
+      return e;
+  size_t idx = 1;
+  cudaEvent_t last = nullptr;
+  for (size_t u0 = 0; u0 < units; u0 += chunk) {
+    const size_t n = units - u0 < chunk ? units - u0 : chunk;
+    cudaEvent_t ein, ek, eout;
+    if ((e = t_pipe.event(dev, idx++, &ein)) != cudaSuccess || (e = t_pipe.event(dev, idx++, &ek)) != cudaSuccess ||
+        (e = t_pipe.event(dev, idx++, &eout)) != cudaSuccess)
+      return e;
+    for (const auto& b : ins)
+      if (b.host_in &&
+          (e = cudaMemcpyAsync(static_cast<char*>(b.dev) + u0 * b.unit_bytes,
+                               static_cast<const char*>(b.host_in) + u0 * b.unit_bytes, n * b.unit_bytes,
+                               cudaMemcpyHostToDevice, si)) != cudaSuccess)
+        return e;
+    if ((e = cudaEventRecord(ein, si)) != cudaSuccess || (e = cudaStreamWaitEvent(s, ein, 0)) != cudaSuccess) return e;
+    if ((e = launch(u0, n)) != cudaSuccess) return e;
+    if ((e = cudaEventRecord(ek, s)) != cudaSuccess || (e = cudaStreamWaitEvent(so, ek, 0)) != cudaSuccess) return e;
+    if ((e = cudaMemcpyAsync(static_cast<char*>(out_buf.host_out) + u0 * out_buf.unit_bytes,
+                             static_cast<const char*>(out_buf.dev) + u0 * out_buf.unit_bytes, n * out_buf.unit_bytes,
+                             cudaMemcpyDeviceToHost, so)) != cudaSuccess ||
+        (e = cudaEventRecord(eout, so)) != cudaSuccess)
+      return e;
+    last = eout;
+  }
+  return last ? cudaStreamWaitEvent(s, last, 0) : cudaSuccess;
+}
 
 // After a synchronizing call, a kernel that gave up a bounded wait shows in the error word.
 lcError_t check_error_word(bool synced) {
@@ -156,6 +254,49 @@ lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* 
   Io io(static_cast<cudaStream_t>(stream));
   const size_t es = elem_size(dtype);
   const size_t bytes = units * seq * head_dim * es;
+  auto attn_args = [&](const void* dq, const void* dk, const void* dv, void* dout, size_t u0, size_t n) {
+    const long long ustride = static_cast<long long>(seq * head_dim);
+    AttnArgs a{};
+    a.q = static_cast<const char*>(dq) + u0 * ustride * es;
+    a.k = static_cast<const char*>(dk) + u0 * ustride * es;
+    a.v = static_cast<const char*>(dv) + u0 * ustride * es;
+    a.out = static_cast<char*>(dout) + u0 * ustride * es;
+    a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = a.out_unit_stride = ustride;
+    a.units = static_cast<int>(n);
+    a.seq = static_cast<int>(seq);
+    a.d = static_cast<int>(head_dim);
+    a.causal = causal ? 1 : 0;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.post_scale = pol.output_scale;
+    a.post_bias = pol.output_bias;
+    a.post_relu = pol.output_relu ? 1 : 0;
+    return a;
+  };
+  const bool any_upload = pol.upload_q || pol.upload_k || pol.upload_v;
+  if (pol.download_out && any_upload && units >= 2 && 4 * bytes >= kPipeMinBytes) {
+    // Host in, host out, large: chunked over units with overlapped copies.
+    void *dq, *dk, *dv, *dout;
+    LC_TRY(pol.upload_q ? io.scratch(bytes, &dq) : (dq = const_cast<void*>(q), cudaSuccess));
+    LC_TRY(pol.upload_k ? io.scratch(bytes, &dk) : (dk = const_cast<void*>(k), cudaSuccess));
+    LC_TRY(pol.upload_v ? io.scratch(bytes, &dv) : (dv = const_cast<void*>(v), cudaSuccess));
+    LC_TRY(io.scratch(bytes, &dout));
+    trace_op(kOpAttention, units * seq * seq * head_dim);
+    const size_t ub = seq * head_dim * es;
+    std::vector<PipeBuf> ins = {{pol.upload_q ? q : nullptr, nullptr, dq, ub},
+                                {pol.upload_k ? k : nullptr, nullptr, dk, ub},
+                                {pol.upload_v ? v : nullptr, nullptr, dv, ub}};
+    PipeBuf ob = {nullptr, out, dout, ub};
+    LC_TRY(run_pipelined(io, units, 1, {}, ins, ob, [&](size_t u0, size_t n) -> cudaError_t {
+      for (size_t c0 = 0; c0 < n; c0 += 65535) {
+        const AttnArgs a = attn_args(dq, dk, dv, dout, u0 + c0, n - c0 < 65535 ? n - c0 : 65535);
+        cudaError_t e = dtype == LC_DTYPE_F32 ? attention_f32(a, io.stream()) : attention_bf16(a, io.stream());
+        if (e != cudaSuccess) return e;
+      }
+      return cudaSuccess;
+    }));
+    LC_TRY(cudaStreamSynchronize(io.stream()));
+    return check_error_word(true);
+  }
   const void *dq, *dk, *dv;
   void* dout;
   LC_TRY(io.in(q, bytes, pol.upload_q, &dq));
@@ -323,6 +464,25 @@ lcError_t lcMatMul(const void* a, const void* b, void* out, size_t m, size_t k, 
   if (policy) pol = *policy;
   Io io(static_cast<cudaStream_t>(stream));
   const size_t es = elem_size(dtype);
+  if (dtype == LC_DTYPE_BF16 && pol.download_out && (pol.upload_a || pol.upload_b) && m >= 512 &&
+      (m * k + k * n + m * n) * es >= kPipeMinBytes) {
+    // Host in, host out, large: B uploaded whole, then A / C row blocks (multiples of 256 rows)
+    // with overlapped copies.
+    void *da, *db, *dc;
+    LC_TRY(pol.upload_a ? io.scratch(m * k * es, &da) : (da = const_cast<void*>(a), cudaSuccess));
+    LC_TRY(pol.upload_b ? io.scratch(k * n * es, &db) : (db = const_cast<void*>(b), cudaSuccess));
+    LC_TRY(io.scratch(m * n * es, &dc));
+    trace_op(kOpMatMul, m * k * n);
+    std::vector<PipeBuf> prefix = {{pol.upload_b ? b : nullptr, nullptr, db, k * n * es}};
+    std::vector<PipeBuf> ins = {{pol.upload_a ? a : nullptr, nullptr, da, k * es}};
+    PipeBuf ob = {nullptr, out, dc, n * es};
+    LC_TRY(run_pipelined(io, m, 256, prefix, ins, ob, [&](size_t r0, size_t rows) -> cudaError_t {
+      return gemm_bf16(static_cast<const __nv_bfloat16*>(da) + r0 * k, static_cast<const __nv_bfloat16*>(db),
+                       static_cast<__nv_bfloat16*>(dc) + r0 * n, (int)rows, (int)k, (int)n, io.stream());
+    }));
+    LC_TRY(cudaStreamSynchronize(io.stream()));
+    return check_error_word(true);
+  }
   const void *da, *db;
   void* dc;
   LC_TRY(io.in(a, m * k * es, pol.upload_a, &da));

@@ -156,6 +156,41 @@ def test_matmul_bf16_each_tc_kernel(gpu, kernel, m, k, n):
     close_enough(ref, out[rows], 2e-3, 2e-2)
 
 
+# ---------------------------------------------------------------- pipelined host staging
+def test_attention_host_pipelined_bf16(gpu):
+    """Host inputs + host output above 24 MB take the chunked path (uploads, kernels and
+    downloads overlapped); results must match the oracle like the single-shot path."""
+    rng = np.random.default_rng(31)
+    units, seq, d = 16, 2048, 128  # 4 x 8 MB of transfers
+    q, k, v = (P.bf16_round(rng.standard_normal((units, seq, d)).astype(np.float32)) for _ in range(3))
+    out = gpu.from_bf16(gpu.attention_batched(bf(gpu, q), bf(gpu, k), bf(gpu, v), causal=True, dtype=gpu.BF16))
+    for u in (0, 7, 15):
+        rows = (0, 1023, 2047)
+        for r in rows:
+            ref = P.attention_rows(q[u], k[u], v[u], True, r, r + 1)
+            close_enough(ref, out[u, r:r + 1], 2e-2, 2e-2)
+
+
+def test_attention_host_pipelined_f32(gpu):
+    rng = np.random.default_rng(32)
+    units, seq, d = 12, 2048, 64  # 4 x 6 MB
+    q, k, v = (rng.standard_normal((units, seq, d)).astype(np.float32) for _ in range(3))
+    out = gpu.attention_batched(q, k, v, causal=True, dtype=gpu.F32)
+    for u in (0, 5, 11):
+        ref = P.attention_rows(q[u], k[u], v[u], True, 1900, 1910)
+        close_enough(ref, out[u, 1900:1910], *F32_TOL)
+
+
+def test_matmul_host_pipelined_bf16(gpu):
+    rng = np.random.default_rng(33)
+    m = k = n = 2048  # 3 x 8 MB
+    a = P.bf16_round((rng.uniform(-1, 1, (m, k)) / np.sqrt(k)).astype(np.float32))
+    b = P.bf16_round(rng.uniform(-1, 1, (k, n)).astype(np.float32))
+    out = gpu.from_bf16(gpu.matmul2d(bf(gpu, a), bf(gpu, b), dtype=gpu.BF16))
+    rows = np.array([0, 255, 256, 1023, 1024, 1535, 2047])
+    close_enough(P.matmul(np.ascontiguousarray(a[rows]), b, threads=8), out[rows], 2e-3, 2e-2)
+
+
 # ---------------------------------------------------------------- graph fused nodes
 @pytest.mark.parametrize("units,seq,d,cols,causal", [(1, 256, 64, 64, 0), (3, 100, 64, 48, 0), (2, 130, 64, 160, 1),
                                                      (1, 77, 32, 8, 0)])
