@@ -18,6 +18,9 @@
 #include <cuda_bf16.h>
 #include <math.h>
 
+#include <string>
+
+#include "../../include/lc_b200.h"
 #include "lc_internal.hpp"
 
 namespace lcb {
@@ -420,7 +423,16 @@ cudaError_t attention_train_dv_update(const float* q, const float* k, float* v, 
   return cudaErrorNotSupported;
 }
 
-cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s) { return dispatch<float>(a, s); }
+cudaError_t attention_f32_simt(const AttnArgs& a, cudaStream_t s) { return dispatch<float>(a, s); }
+
+// fp32 attention: the 3xTF32 tensor-core kernel where it applies (head_dim 64, no LSE output),
+// unless the tune cache pins the SIMT kernel for the shape.
+cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s) {
+  std::string cfg;
+  const bool pinned_simt = tune_lookup(LC_TUNE_ATTENTION, a.seq, a.d, a.causal, LC_DTYPE_F32, &cfg) && cfg == "simt";
+  if (!pinned_simt && attention_f32_tc_supported(a)) return attention_f32_tc(a, s);
+  return attention_f32_simt(a, s);
+}
 cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s) { return dispatch<__nv_bfloat16>(a, s); }
 
 }  // namespace lcb

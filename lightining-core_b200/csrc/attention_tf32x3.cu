@@ -1,0 +1,543 @@
+// Strict-fp32 attention on the 5th-generation tensor cores, head_dim 64 (configs 1 and 5: the
+// reference's fp32 attentionForward, src/attention_cpu.cpp:38-101, and the integrated
+// conv->attention->projection pipeline, python/bindings/bind_integrated.cpp:614-730 with
+// graph.hpp:3529-3547).  fp32 accuracy by the 3xTF32 split of every product:
+//   x = x_hi + x_lo, x_hi = x rounded to tf32, x_lo = x - x_hi (exact in fp32);
+//   x.y ~= x_hi.y_hi + x_hi.y_lo + x_lo.y_hi   (the dropped x_lo.y_lo is ~2^-22 |x y|).
+// A pre-pass writes hi/lo planes of Q and K ([units, S, 64]) and of V transposed ([units, 64, Sp],
+// Sp = S rounded up to 4), so every MMA operand is K-major in shared memory.
+//
+// One CTA = one 128-row Q tile, one CTA per SM (192 KB of shared memory), 224 threads:
+//   warp 0      TMA: Q hi/lo once, K hi/lo tiles (64 keys) into a 2-stage ring freed by S_j;
+//               warp 6: V^T hi/lo tiles into a 2-stage ring freed by P.V_j.
+//   warp 1      MMA: S_j = Q K_j^T (3 x 8 tcgen05.mma.kind::tf32, M=128 N=64 K=8) into one of two
+//               TMEM score buffers; O_j = P_j V_j (3 x 8 MMAs with P read from TMEM) into one of
+//               two TMEM buffers, a fresh partial per tile.
+//   warps 2..5  softmax, one query row per thread: scores into registers, running max m (lazy:
+//               rescale only when it grows by more than 2^8), p = 2^(s*scale*log2e - m), l += p,
+//               P_hi over S_j's own columns and P_lo into its own buffer; then the previous
+//               tile's O partial is folded into 64 per-row fp32 registers, O = O*alpha + O_tile
+//               (round-to-nearest adds: the tensor core's long fp32 accumulations drift).  The
+//               epilogue divides by l, applies the optional projection out = O @ W (W [64, cols])
+//               and the postprocess, and writes fp32 rows.
+// Every mbarrier wait is bounded (common.cuh).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "../../include/lc_b200.h"
+#include "common.cuh"
+#include "lc_internal.hpp"
+
+namespace lcb {
+
+void* tensor_map_encoder();
+
+namespace {
+
+constexpr int D = 64;
+constexpr int TILE = 128;
+constexpr int TK = 64;
+constexpr int NUM_THREADS = 224;
+constexpr int QCH = TILE * 128;       // one [128 rows x 32 fp32] swizzled chunk = 16 KB
+constexpr int KCH = TK * 128;         // [64 keys x 32 fp32] = 8 KB
+constexpr int VCH = D * 128;          // [64 d-rows x 32 keys] = 8 KB
+constexpr int Q_PLANE = 2 * QCH;      // 32 KB (64 d)
+constexpr int K_PLANE = 2 * KCH;      // 16 KB
+constexpr int V_PLANE = 2 * VCH;      // 16 KB (64 keys)
+constexpr int Q_OFF = 0;              // Q_hi, Q_lo
+constexpr int K_OFF = 2 * Q_PLANE;    // 2 stages x (K_hi, K_lo)
+constexpr int V_OFF = K_OFF + 2 * 2 * K_PLANE;
+constexpr int TAIL_OFF = V_OFF + 2 * 2 * V_PLANE;
+constexpr uint32_t S_COL = 0, PL_COL = 128, O_COL = 256, TMEM_COLS = 512;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;
+constexpr uint32_t IDESC = idesc_tf32_f32(TILE, 64, 0, 0);  // S (N = 64 keys) and O (N = D = 64)
+
+struct Tail {
+  uint64_t q_full;
+  uint64_t k_full[2], v_full[2];
+  uint64_t s_full[2];   // S_j in TMEM (the S group's only commit)
+  uint64_t p_full[2];   // P_hi/P_lo of tile j in TMEM (4 warp arrivals)
+  uint64_t o_full[2];   // the O partial of tile j in TMEM (the P.V group's only commit)
+  uint64_t o_free[2];   // the softmax warps have folded that partial (4 arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = 1024 + TAIL_OFF + sizeof(Tail);
+
+struct Params {
+  float* out;
+  long long out_unit_stride;
+  int units, seq, nq;
+  int causal;
+  float scale_log2;
+  float post_scale, post_bias;
+  int post_relu, post;
+  const float* proj_w;
+  int cols;  // output columns: D, or proj_cols with a projection
+  unsigned* err_word;
+};
+
+__device__ __forceinline__ float tf32_round(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
+  return __uint_as_float(u);
+}
+
+// 2^x, MUFU ex2 without flush-to-zero (relative error ~2^-22).
+__device__ __forceinline__ float exp2_acc(float x) {
+  float y;
+  asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* err,
+                                          unsigned code) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, err, code) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+// ---- pre-pass -----------------------------------------------------------------------------------
+// Rows of 64 floats (unit u at src + u*unit_stride) -> contiguous hi/lo planes [units, S, 64].
+__global__ void split_rows_kernel(const float* __restrict__ src, long long unit_stride, float* __restrict__ hi,
+                                  float* __restrict__ lo, int units, int seq) {
+  const long long total = static_cast<long long>(units) * seq * D;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long u = i / (static_cast<long long>(seq) * D);
+    const long long r = i - u * seq * D;
+    const float v = src[u * unit_stride + r];
+    const float h = tf32_round(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+// V [units][S][64] (unit stride) -> hi/lo planes of V^T [units][64][Sp], zero for keys >= S.
+__global__ void split_vt_kernel(const float* __restrict__ v, long long unit_stride, float* __restrict__ hi_t,
+                                float* __restrict__ lo_t, int seq, int sp) {
+  __shared__ float tile[32][33];
+  const int u = blockIdx.z;
+  const int k0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const float* vu = v + static_cast<long long>(u) * unit_stride;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int k = k0 + r;
+    tile[r][threadIdx.x] = k < seq ? vu[static_cast<long long>(k) * D + d0 + threadIdx.x] : 0.0f;
+  }
+  __syncthreads();
+  float* hu = hi_t + static_cast<long long>(u) * D * sp;
+  float* lu = lo_t + static_cast<long long>(u) * D * sp;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int d = d0 + r, k = k0 + threadIdx.x;
+    if (k < sp) {
+      const float x = tile[threadIdx.x][r];
+      const float h = tf32_round(x);
+      hu[static_cast<long long>(d) * sp + k] = h;
+      lu[static_cast<long long>(d) * sp + k] = x - h;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fa_f32_tc_kernel(const __grid_constant__ CUtensorMap map_qh, const __grid_constant__ CUtensorMap map_ql,
+                     const __grid_constant__ CUtensorMap map_kh, const __grid_constant__ CUtensorMap map_kl,
+                     const __grid_constant__ CUtensorMap map_vh, const __grid_constant__ CUtensorMap map_vl,
+                     const Params p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Tail* st = reinterpret_cast<Tail*>(smem + TAIL_OFF);
+  uint8_t* sQh = smem + Q_OFF;
+  uint8_t* sQl = sQh + Q_PLANE;
+  auto sK = [&](int stage, int lo) { return smem + K_OFF + (stage * 2 + lo) * K_PLANE; };
+  auto sV = [&](int stage, int lo) { return smem + V_OFF + (stage * 2 + lo) * V_PLANE; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qt = p.nq - 1 - static_cast<int>(blockIdx.x) % p.nq;
+  const int unit = static_cast<int>(blockIdx.x) / p.nq;
+  const int q0 = qt * TILE;
+  const int kv_all = (p.seq + TK - 1) / TK;
+  const int n_kv = p.causal ? min(kv_all, (q0 + TILE - 1) / TK + 1) : kv_all;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&st->q_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&st->k_full[b], 1);
+      mbar_init(&st->v_full[b], 1);
+      mbar_init(&st->s_full[b], 1);
+      mbar_init(&st->p_full[b], 4);
+      mbar_init(&st->o_full[b], 1);
+      mbar_init(&st->o_free[b], 4);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init();
+    mbar_arrive_expect_tx(&st->q_full, 2 * Q_PLANE);
+    for (int c = 0; c < 2; ++c) {
+      tma_load_3d(sQh + c * QCH, &map_qh, c * 32, q0, unit, &st->q_full);
+      tma_load_3d(sQl + c * QCH, &map_ql, c * 32, q0, unit, &st->q_full);
+    }
+  }
+  if (warp == 0) {
+    tmem_alloc(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+  auto drain = [](uint64_t* bar, uint32_t ph) {
+    const uint64_t t1 = globaltimer_ns();
+    while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t1 < 100000000ull) {
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ K loads
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        // Slot s last held K_{j-2}; S_{j-2} (single commit: s_full[j&1]) must be done.  S_j needs
+        // the load issued here, so the parity wait is unambiguous.
+        if (j >= 2 && !mbar_wait_bounded(&st->s_full[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&st->k_full[s], 2 * K_PLANE);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(sK(s, 0) + c * KCH, &map_kh, c * 32, j * TK, unit, &st->k_full[s]);
+          tma_load_3d(sK(s, 1) + c * KCH, &map_kl, c * 32, j * TK, unit, &st->k_full[s]);
+        }
+        ++issued;
+      }
+      if (!ok) {
+        drain(&st->q_full, 0);
+        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) drain(&st->k_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 6) {
+    // ------------------------------------------------------------ V^T loads
+    if (lane == 0) {
+      bool ok = true;
+      int issued = 0;
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        // Slot s last held V_{j-2}; P.V_{j-2} (single commit: o_full[j&1]) must be done.
+        if (j >= 2 && !mbar_wait_bounded(&st->o_full[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&st->v_full[s], 2 * V_PLANE);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(sV(s, 0) + c * VCH, &map_vh, j * TK + c * 32, 0, unit, &st->v_full[s]);
+          tma_load_3d(sV(s, 1) + c * VCH, &map_vl, j * TK + c * 32, 0, unit, &st->v_full[s]);
+        }
+        ++issued;
+      }
+      if (!ok)
+        for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) drain(&st->v_full[j & 1], (j >> 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issue
+    if (lane == 0) {
+      bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
+      bool issued = false;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait_bounded(&st->k_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem + S_COL + static_cast<uint32_t>(s * TK);
+        const uint32_t qh = smem_u32(sQh), ql = smem_u32(sQl);
+        const uint32_t kh = smem_u32(sK(s, 0)), kl = smem_u32(sK(s, 1));
+#pragma unroll
+        for (int kk = 0; kk < D / 8; ++kk) {
+          const uint32_t qo = (kk >> 2) * QCH + (kk & 3) * 32, ko = (kk >> 2) * KCH + (kk & 3) * 32;
+          umma_tf32_ss(d, smem_desc_sw128(ql + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC,
+                       kk > 0 ? 1u : 0u);
+          umma_tf32_ss(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kl + ko, 16, 1024), IDESC, 1u);
+          umma_tf32_ss(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC, 1u);
+        }
+        issued = true;
+        umma_commit(&st->s_full[s]);  // the only commit of this group
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        if (j + 1 < n_kv && !issue_s(j + 1)) {
+          ok = false;
+          break;
+        }
+        // p_full[s] next completes for P_{j+2}, which needs S_{j+2} (issued after this wait);
+        // v_full[s] next completes after this P.V; o_free[s] next completes for the fold of
+        // tile j, which needs this P.V.
+        if (!mbar_wait_bounded(&st->p_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !mbar_wait_bounded(&st->v_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            (j >= 2 &&
+             !mbar_wait_bounded(&st->o_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t o = tmem + O_COL + static_cast<uint32_t>(s * D);
+        const uint32_t ph = tmem + S_COL + static_cast<uint32_t>(s * TK);   // P_hi over S_j
+        const uint32_t pl = tmem + PL_COL + static_cast<uint32_t>(s * TK);  // P_lo
+        const uint32_t vh = smem_u32(sV(s, 0)), vl = smem_u32(sV(s, 1));
+#pragma unroll
+        for (int kk = 0; kk < TK / 8; ++kk) {
+          const uint32_t vo = (kk >> 2) * VCH + (kk & 3) * 32;
+          umma_tf32_ts(o, pl + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          umma_tf32_ts(o, ph + kk * 8, smem_desc_sw128(vl + vo, 16, 1024), IDESC, 1u);
+          umma_tf32_ts(o, ph + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, 1u);
+        }
+        umma_commit(&st->o_full[s]);  // the only commit of this group
+      }
+      if (!ok && issued) {
+        umma_commit(&st->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else if (warp >= 2 && warp <= 5) {
+    // ------------------------------------------------------------ softmax, fold, epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
+    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
+    float o_acc[D];
+#pragma unroll
+    for (int e = 0; e < D; ++e) o_acc[e] = 0.0f;
+    bool ok = true;
+    // Folds the O partial of tile t (in buffer t&1) into the registers: o = o * alpha + O_t.
+    auto fold = [&](int t, float alpha) -> bool {
+      // o_full[t&1] next completes for P.V_{t+2}, which needs this fold's o_free first.
+      if (!warp_wait(&st->o_full[t & 1], (t >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) return false;
+      tc_fence_after();
+      const uint32_t ob = tmem + lane_base + O_COL + static_cast<uint32_t>((t & 1) * D);
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(ob + c, r);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o_acc[c + e] = __fmaf_rn(o_acc[c + e], alpha, __uint_as_float(r[e]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->o_free[t & 1]);
+      return true;
+    };
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      // s_full[s] next completes for S_{j+2}, which needs P_j from these warps first.
+      if (!warp_wait(&st->s_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t sb = tmem + lane_base + S_COL + static_cast<uint32_t>(s * TK);
+      uint32_t r[TK];
+      {
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(r);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(r + 32);
+        tmem_ld32(sb, r0);
+        tmem_ld32(sb + 32, r1);
+      }
+      const int kv0 = j * TK;
+      if (kv0 + TK - 1 > kmax) {
+#pragma unroll
+        for (int e = 0; e < TK; ++e)
+          if (kv0 + e > kmax) r[e] = __float_as_uint(-INFINITY);
+      }
+      float mx = __uint_as_float(r[0]);
+#pragma unroll
+      for (int e = 1; e < TK; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+      mx *= p.scale_log2;
+      float alpha = 1.0f;
+      if (mx > m + RESCALE_THRESHOLD) {
+        alpha = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
+        l *= alpha;
+        m = mx;
+      }
+      // P_j: p = 2^(s*scale*log2e - m) in fp32; P_hi over S_j's columns, P_lo into its buffer.
+      // The last reader of both buffers before this was P.V_{j-2}, issued before S_j.
+      float lsum = 0.0f;
+#pragma unroll
+      for (int g = 0; g < TK / 16; ++g) {
+        uint32_t wh[16], wl[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float pv = exp2_acc(__fmaf_rn(__uint_as_float(r[g * 16 + i]), p.scale_log2, -m));
+          const float ph = tf32_round(pv);
+          lsum += pv;
+          wh[i] = __float_as_uint(ph);
+          wl[i] = __float_as_uint(pv - ph);
+        }
+        tmem_st16(sb + g * 16, wh);
+        tmem_st16(tmem + lane_base + PL_COL + static_cast<uint32_t>(s * TK + g * 16), wl);
+      }
+      l += lsum;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->p_full[s]);
+      // Fold the previous tile's partial (computed with the previous max), then remember this
+      // tile's rescale factor for its own fold.
+      if (j > 0 && !fold(j - 1, alpha_prev)) {
+        ok = false;
+        break;
+      }
+      alpha_prev = alpha;
+    }
+    if (ok && fold(n_kv - 1, alpha_prev) && qrow < p.seq) {
+      const float inv = 1.0f / l;
+      float* orow = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(qrow) * p.cols;
+      if (p.proj_w) {
+        for (int c = 0; c < p.cols; ++c) {
+          float acc = 0.0f;
+#pragma unroll
+          for (int e = 0; e < D; ++e) acc = __fmaf_rn(o_acc[e] * inv, __ldg(p.proj_w + e * p.cols + c), acc);
+          orow[c] = acc;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < D; e += 4) {
+          float y[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float v = o_acc[e + i] * inv;
+            if (p.post) {
+              v = v * p.post_scale + p.post_bias;
+              if (p.post_relu && v < 0.0f) v = 0.0f;
+            }
+            y[i] = v;
+          }
+          reinterpret_cast<float4*>(orow)[e / 4] = make_float4(y[0], y[1], y[2], y[3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// fp32 [units, rows, cols] (contiguous), box [1, box_rows, 32], 128-byte swizzle, zero fill.
+bool make_tmap_f32_3d(CUtensorMap* map, const void* base, int units, int rows, int cols, int box_rows) {
+  auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
+  if (!enc) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(units)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 4, static_cast<cuuint64_t>(rows) * cols * 4};
+  cuuint32_t box[3] = {32, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool attention_f32_tc_supported(const AttnArgs& a) {
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  const int cols = a.proj_w ? a.proj_cols : a.d;
+  return a.d == D && a.lse == nullptr && a.seq >= 1 && cols >= 1 && cols <= 256 && al(a.out) &&
+         (a.out_unit_stride % 4) == 0 && (cols % 4 == 0 || a.proj_w != nullptr) &&
+         !(a.proj_w && a.post_relu) && tensor_map_encoder() != nullptr;
+}
+
+cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  const int sp = (a.seq + 3) & ~3;
+  const size_t nqk = static_cast<size_t>(a.units) * a.seq * D, nv = static_cast<size_t>(a.units) * D * sp;
+  const size_t bytes = (4 * nqk + 2 * nv) * sizeof(float);
+  // Split planes in a grow-only per-device workspace; `attn_tf32_done` orders the launches
+  // that use it one after another, whatever their streams.
+  std::lock_guard<std::mutex> lk(ctx->attn_tf32_mu);
+  cudaError_t e = cudaSuccess;
+  if (!ctx->attn_tf32_done) e = cudaEventCreateWithFlags(&ctx->attn_tf32_done, cudaEventDisableTiming);
+  if (e != cudaSuccess) return e;
+  if (ctx->attn_tf32_bytes < bytes) {
+    if (ctx->attn_tf32_ws) {
+      if ((e = cudaEventSynchronize(ctx->attn_tf32_done)) != cudaSuccess) return e;
+      cudaFree(ctx->attn_tf32_ws);
+      ctx->attn_tf32_ws = nullptr;
+      ctx->attn_tf32_bytes = 0;
+    }
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->attn_tf32_ws), bytes)) != cudaSuccess) return e;
+    ctx->attn_tf32_bytes = bytes;
+  }
+  float* qh = ctx->attn_tf32_ws;
+  float* ql = qh + nqk;
+  float* kh = ql + nqk;
+  float* kl = kh + nqk;
+  float* vh = kl + nqk;
+  float* vl = vh + nv;
+  CUtensorMap mqh, mql, mkh, mkl, mvh, mvl;
+  if (!make_tmap_f32_3d(&mqh, qh, a.units, a.seq, D, TILE) || !make_tmap_f32_3d(&mql, ql, a.units, a.seq, D, TILE) ||
+      !make_tmap_f32_3d(&mkh, kh, a.units, a.seq, D, TK) || !make_tmap_f32_3d(&mkl, kl, a.units, a.seq, D, TK) ||
+      !make_tmap_f32_3d(&mvh, vh, a.units, D, sp, D) || !make_tmap_f32_3d(&mvl, vl, a.units, D, sp, D))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent
+  if (!attr_set) {
+    if ((e = cudaFuncSetAttribute(fa_f32_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(SMEM_BYTES))) != cudaSuccess)
+      return e;
+    attr_set = true;
+  }
+  if ((e = cudaStreamWaitEvent(s, ctx->attn_tf32_done, 0)) != cudaSuccess) return e;
+  const int blocks = static_cast<int>(std::min<size_t>(nqk / 256 + 1, 148 * 8));
+  split_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.units, a.seq);
+  split_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.units, a.seq);
+  split_vt_kernel<<<dim3((sp + 31) / 32, D / 32, a.units), dim3(32, 8), 0, s>>>(static_cast<const float*>(a.v),
+                                                                                a.v_unit_stride, vh, vl, a.seq, sp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  Params p;
+  p.out = static_cast<float*>(a.out);
+  p.out_unit_stride = a.out_unit_stride;
+  p.units = a.units;
+  p.seq = a.seq;
+  p.nq = (a.seq + TILE - 1) / TILE;
+  p.causal = a.causal;
+  p.scale_log2 = a.scale * LOG2E;
+  p.post_scale = a.post_scale;
+  p.post_bias = a.post_bias;
+  p.post_relu = a.post_relu;
+  p.post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
+  p.proj_w = a.proj_w;
+  p.cols = a.proj_w ? a.proj_cols : D;
+  p.err_word = ctx->err_word;
+  const long long grid = static_cast<long long>(p.nq) * a.units;
+  if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  fa_f32_tc_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return cudaEventRecord(ctx->attn_tf32_done, s);
+}
+
+}  // namespace lcb

@@ -116,7 +116,7 @@ extern "C" lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, 
     a.post_scale = 1.0f;
     a.proj_w = proj_w;
     a.proj_cols = static_cast<int>(proj_cols);
-    e = attention_f32(a, s);
+    e = attention_f32_simt(a, s);  // the tensor-core path would allocate its split planes
     if (e != cudaSuccess) return from_cuda(e);
   }
   return LC_SUCCESS;

@@ -21,6 +21,11 @@ struct DeviceCtx {
   float* tf32_ws = nullptr;
   size_t tf32_ws_bytes = 0;
   cudaEvent_t tf32_done = nullptr;
+  // Split planes of the 3xTF32 fp32 attention (grow-only), ordered the same way.
+  std::mutex attn_tf32_mu;
+  float* attn_tf32_ws = nullptr;
+  size_t attn_tf32_bytes = 0;
+  cudaEvent_t attn_tf32_done = nullptr;
 };
 DeviceCtx* device_ctx();
 
@@ -81,6 +86,11 @@ struct AttnArgs {
   float* lse;            // optional [units, seq] log-sum-exp of the scaled scores (fp32 path only)
 };
 cudaError_t attention_f32(const AttnArgs& a, cudaStream_t s);
+// The SIMT fp32 kernels (any head_dim <= 256, LSE output, fused projection); never allocates.
+cudaError_t attention_f32_simt(const AttnArgs& a, cudaStream_t s);
+// Strict fp32 attention on tcgen05 by the 3xTF32 split (attention_tf32x3.cu), head_dim 64.
+bool attention_f32_tc_supported(const AttnArgs& a);
+cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s);
 // Train step pieces (fp32): dO = 2(O - T)/(seq*d) and per-unit sum of squared errors (double);
 // then dV = P^T dO recomputed from Q, K and the forward's LSE, applied as v -= lr * dV in place.
 cudaError_t attention_train_grad_out(const float* out, const float* target, float* dout, double* sse, int units,

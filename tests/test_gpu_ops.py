@@ -156,6 +156,23 @@ def test_matmul_bf16_each_tc_kernel(gpu, kernel, m, k, n):
     close_enough(ref, out[rows], 2e-3, 2e-2)
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05_3xtf32", "simt"])
+@pytest.mark.parametrize("units,seq,causal", [(1, 256, 0), (3, 777, 1), (2, 100, 0)])
+def test_attention_f32_each_kernel(gpu, kernel, units, seq, causal):
+    """Strict fp32 attention (head_dim 64) on the 3xTF32 tensor-core kernel (the default) and on
+    the SIMT kernel (pinned through the tune cache), both within 1e-4 of the reference loop."""
+    rng = np.random.default_rng(units * 100 + seq)
+    q, k, v = (rng.standard_normal((units, seq, 64)).astype(np.float32) for _ in range(3))
+    if kernel == "simt":
+        gpu.tune_cache_set(gpu.TUNE_ATTENTION, seq, 64, causal, "simt", gpu.F32)
+    try:
+        out = gpu.attention_batched(q, k, v, causal=bool(causal), dtype=gpu.F32)
+    finally:
+        gpu.tune_cache_reset(gpu.TUNE_ATTENTION)
+    for u in range(units):
+        close_enough(P.attention(q[u], k[u], v[u], bool(causal)), out[u], *F32_TOL)
+
+
 # ---------------------------------------------------------------- pipelined host staging
 def test_attention_host_pipelined_bf16(gpu):
     """Host inputs + host output above 24 MB take the chunked path (uploads, kernels and
