@@ -85,7 +85,7 @@ extern "C" lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, 
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return from_cuda(e);
   float* conv = scratch;
-  e = conv2d_nchw_f32(x, w, bias, conv, (int)batch, (int)in_channels, (int)in_h, (int)in_w, (int)out_channels,
+  e = conv2d_nchw_f32_simt(x, w, bias, conv, (int)batch, (int)in_channels, (int)in_h, (int)in_w, (int)out_channels,
                       (int)kernel_h, (int)kernel_w, (int)stride_h, (int)stride_w, (int)pad_h, (int)pad_w, 1, s);
   if (e != cudaSuccess) return from_cuda(e);
   const float* qkv = conv;

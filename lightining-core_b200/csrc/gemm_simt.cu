@@ -230,9 +230,9 @@ cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_
              n, k, s);
 }
 
-cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
-                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
-                            cudaStream_t s) {
+cudaError_t conv2d_nchw_f32_simt(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                                 int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
+                                 int relu, cudaStream_t s) {
   const int oh = (in_h + 2 * ph - kh) / sh + 1;
   const int ow = (in_w + 2 * pw - kw) / sw + 1;
   const int rows = batch * oh * ow;

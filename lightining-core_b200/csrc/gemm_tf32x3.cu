@@ -82,6 +82,46 @@ __global__ void tf32_split_transpose_kernel(const float* __restrict__ b, float* 
   }
 }
 
+// Rows of src [rows, k] -> hi/lo planes [rows, kp] (kp >= k, zero padded).
+__global__ void tf32_split_rows_pad_kernel(const float* __restrict__ src, float* __restrict__ hi,
+                                           float* __restrict__ lo, int rows, int k, int kp) {
+  const long long total = static_cast<long long>(rows) * kp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / kp;
+    const int c = static_cast<int>(i - r * kp);
+    const float v = c < k ? src[r * k + c] : 0.0f;
+    const float h = tf32_round(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
+// im2col of an NCHW input as the K-major B^T planes of the conv GEMM: row j = (image, oh, ow),
+// column kk = (c, kh, kw) (the OIHW weight order), zero outside the padded input and for kk >= k.
+__global__ void tf32_im2col_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                         int rows, int k, int kp, int in_c, int in_h, int in_w, int kh, int kw, int sh,
+                                         int sw, int ph, int pw, int oh, int ow) {
+  const long long total = static_cast<long long>(rows) * kp;
+  const int pix = oh * ow;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int j = static_cast<int>(i / kp);
+    const int kk = static_cast<int>(i - static_cast<long long>(j) * kp);
+    float v = 0.0f;
+    if (kk < k) {
+      const int n = j / pix, pp = j - n * pix;
+      const int y = pp / ow, xo = pp - y * ow;
+      const int c = kk / (kh * kw), r = kk - c * kh * kw;
+      const int dy = r / kw, dx = r - dy * kw;
+      const int iy = y * sh + dy - ph, ix = xo * sw + dx - pw;
+      if (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
+        v = x[((static_cast<long long>(n) * in_c + c) * in_h + iy) * in_w + ix];
+    }
+    const float h = tf32_round(v);
+    hi[i] = h;
+    lo[i] = v - h;
+  }
+}
+
 // hi = tf32(x), lo = x - hi, four elements per thread.
 __global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
                                   size_t n4) {
@@ -123,7 +163,8 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
-                       float* __restrict__ C, int M, int N, int K, unsigned* err_word) {
+                       float* __restrict__ C, int M, int N, int K, int period, long long batch_stride,
+                       long long row_stride, const float* __restrict__ row_bias, int relu, unsigned* err_word) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // Stage layout: A_hi | A_lo | B_hi | B_lo.
@@ -272,7 +313,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const bool vec_ok = (N % 4) == 0;
+    // Vector stores need every segment start 16-byte aligned.
+    const bool vec_ok = (period % 4) == 0 && (row_stride % 4) == 0 && (batch_stride % 4) == 0 &&
+                        (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
     const int chunks = (num_kb + CHUNK_KB - 1) / CHUNK_KB;
     bool ok = true;
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
@@ -306,18 +349,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok) break;
+      // Element (row, col) goes to C + (col / period) * batch_stride + row * row_stride + col % period:
+      // a plain row-major C (period = N), or NCHW conv output (period = OH*OW pixels of an image).
       const int row = mb * BM + row_in_tile;
       if (row < M) {
-        float* crow = C + static_cast<long long>(row) * N + nb * BN;
-        const int left = N - nb * BN;
-        if (vec_ok && left >= BN) {
+        const float bias = row_bias ? __ldg(row_bias + row) : 0.0f;
+        if (row_bias || relu) {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) {
+            float v = sum[j] + bias;
+            sum[j] = relu ? fmaxf(v, 0.0f) : v;
+          }
+        }
+        const int col0 = nb * BN;
+        const int img = col0 / period, pix = col0 - img * period;
+        float* dst = C + static_cast<long long>(img) * batch_stride + static_cast<long long>(row) * row_stride + pix;
+        if (vec_ok && col0 + BN <= N && pix + BN <= period) {
 #pragma unroll
           for (int q = 0; q < BN / 4; ++q)
-            reinterpret_cast<float4*>(crow)[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+            reinterpret_cast<float4*>(dst)[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN; ++j)
-            if (j < left) crow[j] = sum[j];
+          for (int j = 0; j < BN; ++j) {
+            const int col = col0 + j;
+            if (col < N) {
+              const int im = col / period;
+              C[static_cast<long long>(im) * batch_stride + static_cast<long long>(row) * row_stride +
+                (col - im * period)] = sum[j];
+            }
+          }
         }
       }
     }
@@ -365,57 +425,119 @@ bool gemm_f32_tc_supported(const void* a, const void* b, const void* c, int m, i
          tensor_map_encoder() != nullptr;
 }
 
-cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
-  DeviceCtx* ctx = device_ctx();
-  if (!ctx) return cudaErrorNoDevice;
-  const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
-  const size_t bytes = 2 * (na + nb) * sizeof(float);
-  // The split planes live in a grow-only per-device workspace; `tf32_done` orders every launch
-  // that uses it after the previous one, whatever its stream.
-  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
+namespace {
+
+struct Epi {
+  float* c;
+  int period;
+  long long batch_stride, row_stride;
+  const float* row_bias;
+  int relu;
+};
+
+// Workspace of at least `bytes`, ordered after the previous 3xTF32 launch (caller holds tf32_mu).
+cudaError_t tf32_workspace(DeviceCtx* ctx, size_t bytes, cudaStream_t s) {
   cudaError_t e = cudaSuccess;
-  if (!ctx->tf32_done) e = cudaEventCreateWithFlags(&ctx->tf32_done, cudaEventDisableTiming);
-  if (e != cudaSuccess) return e;
+  if (!ctx->tf32_done && (e = cudaEventCreateWithFlags(&ctx->tf32_done, cudaEventDisableTiming)) != cudaSuccess)
+    return e;
   if (ctx->tf32_ws_bytes < bytes) {
     if (ctx->tf32_ws) {
-      e = cudaEventSynchronize(ctx->tf32_done);
-      if (e != cudaSuccess) return e;
+      if ((e = cudaEventSynchronize(ctx->tf32_done)) != cudaSuccess) return e;
       cudaFree(ctx->tf32_ws);
       ctx->tf32_ws = nullptr;
       ctx->tf32_ws_bytes = 0;
     }
-    e = cudaMalloc(reinterpret_cast<void**>(&ctx->tf32_ws), bytes);
-    if (e != cudaSuccess) return e;
+    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->tf32_ws), bytes)) != cudaSuccess) return e;
     ctx->tf32_ws_bytes = bytes;
   }
+  return cudaStreamWaitEvent(s, ctx->tf32_done, 0);
+}
+
+// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each), then the event that
+// releases the workspace.
+cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                          int m, int n, int kp, const Epi& epi, cudaStream_t s) {
+  CUtensorMap mah, mal, mbh, mbl;
+  if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
+      !make_tmap_f32_2d(&mbh, b_hi, n, kp, BN, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, BN, BK))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent attribute set
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
+  gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mah, mal, mbh, mbl, epi.c, m, n, kp, epi.period,
+                                                           epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+                                                           ctx->err_word);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) e = cudaEventRecord(ctx->tf32_done, s);
+  return e;
+}
+
+int grid_for(long long n) { return static_cast<int>(n / 256 + 1 < 148 * 8 ? n / 256 + 1 : 148 * 8); }
+
+}  // namespace
+
+cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
+  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
+  cudaError_t e = tf32_workspace(ctx, 2 * (na + nb) * sizeof(float), s);
+  if (e != cudaSuccess) return e;
   float* a_hi = ctx->tf32_ws;
   float* a_lo = a_hi + na;
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
-  CUtensorMap mah, mal, mbh, mbl;
-  if (!make_tmap_f32_2d(&mah, a_hi, m, k, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, k, BM, BK) ||
-      !make_tmap_f32_2d(&mbh, b_hi, n, k, BN, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, k, BN, BK))
-    return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent attribute set
-  if (!attr_set) {
-    e = cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
-  e = cudaStreamWaitEvent(s, ctx->tf32_done, 0);
-  if (e == cudaSuccess) e = split(a, a_hi, a_lo, na, s);
-  if (e == cudaSuccess) {
-    tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
-    e = cudaGetLastError();
-  }
+  if ((e = split(a, a_hi, a_lo, na, s)) != cudaSuccess) return e;
+  tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s);
+}
+
+// Conv as out_n[oc, p] = sum_kk W[oc, kk] col_n[kk, p] for all images at once: A = W [OC, C*kh*kw]
+// (OIHW as is), B^T = the im2col rows [images*OH*OW, C*kh*kw]; the epilogue writes NCHW with
+// bias and ReLU.  The reduction dimension is zero-padded to a multiple of 4 (TMA row pitch).
+cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                                   int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
+                                   int relu, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  const int oh = (in_h + 2 * ph - kh) / sh + 1, ow = (in_w + 2 * pw - kw) / sw + 1;
+  const int k = in_c * kh * kw, kp = (k + 3) & ~3;
+  const long long rows = static_cast<long long>(batch) * oh * ow;
+  if (rows > 0x7fffffffLL) return cudaErrorNotSupported;
+  const size_t na = static_cast<size_t>(out_c) * kp, nb = static_cast<size_t>(rows) * kp;
+  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
+  cudaError_t e = tf32_workspace(ctx, 2 * (na + nb) * sizeof(float), s);
   if (e != cudaSuccess) return e;
-  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
-  const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-  gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mah, mal, mbh, mbl, c, m, n, k, ctx->err_word);
-  e = cudaGetLastError();
-  if (e == cudaSuccess) e = cudaEventRecord(ctx->tf32_done, s);
-  return e;
+  float* a_hi = ctx->tf32_ws;
+  float* a_lo = a_hi + na;
+  float* b_hi = a_lo + na;
+  float* b_lo = b_hi + nb;
+  tf32_split_rows_pad_kernel<<<grid_for(static_cast<long long>(na)), 256, 0, s>>>(w, a_hi, a_lo, out_c, k, kp);
+  tf32_im2col_split_kernel<<<grid_for(static_cast<long long>(nb)), 256, 0, s>>>(
+      x, b_hi, b_lo, static_cast<int>(rows), k, kp, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  const int pix = oh * ow;
+  return launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, out_c, static_cast<int>(rows), kp,
+                       Epi{out, pix, static_cast<long long>(out_c) * pix, pix, bias, relu}, s);
+}
+
+// fp32 conv: the 3xTF32 tensor-core GEMM once the work covers its pre-pass (>= 2^28
+// multiply-adds), else the SIMT implicit GEMM.
+cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
+                            cudaStream_t s) {
+  const long long oh = (in_h + 2 * ph - kh) / sh + 1, ow = (in_w + 2 * pw - kw) / sw + 1;
+  const long long macs = static_cast<long long>(out_c) * batch * oh * ow * in_c * kh * kw;
+  if (macs >= (1LL << 28) && out_c >= 32 && tensor_map_encoder() != nullptr)
+    return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
+  return conv2d_nchw_f32_simt(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
 }
 
 }  // namespace lcb

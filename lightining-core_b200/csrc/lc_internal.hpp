@@ -67,6 +67,14 @@ cudaError_t gemm_bf16_tc2(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_b
 cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
                             int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
                             int relu, cudaStream_t s);
+// The SIMT implicit-GEMM conv (never allocates) and the 3xTF32 tensor-core conv (split planes in
+// the device's 3xTF32 workspace); conv2d_nchw_f32 picks by size.
+cudaError_t conv2d_nchw_f32_simt(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
+                            int relu, cudaStream_t s);
+cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                            int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
+                            int relu, cudaStream_t s);
 // Cyclic repeat of the first `have` floats of src into dst[0, total) (qkv_pack short case).
 cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s);
 
