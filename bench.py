@@ -228,8 +228,19 @@ def run_ours(args, rank, world, local_rank):
         return lambda: lc.check(L.lcMatMul(C.c_void_p(fa.data_ptr()), C.c_void_p(fb.data_ptr()),
                                            C.c_void_p(fc.data_ptr()), n, n, n, lc.F32, None, sp), "matmul f32")
 
+    def f32attn_fn():
+        # Strict fp32 attention at the config-5 shape ([32, 3136, 64], non-causal), 3xTF32 path.
+        g.manual_seed(4)
+        fq, fk, fv = (torch.randn((32, 3136, 64), generator=g, device=dev) for _ in range(3))
+        fo = torch.empty_like(fq)
+        return lambda: lc.check(L.lcAttentionForward(C.c_void_p(fq.data_ptr()), C.c_void_p(fk.data_ptr()),
+                                                     C.c_void_p(fv.data_ptr()), C.c_void_p(fo.data_ptr()), 32, 3136,
+                                                     64, 0, lc.F32, None, sp), "attention f32")
+
     if args.only:
-        fn = {"gemm": gemm, "attention": attn, "f32gemm": None}[args.only] or f32gemm_fn()
+        fn = {"gemm": gemm, "attention": attn, "f32gemm": None, "f32attn": None}[args.only]
+        if fn is None:
+            fn = f32gemm_fn() if args.only == "f32gemm" else f32attn_fn()
         for _ in range(args.warmup + args.steps):
             fn()
         torch.cuda.synchronize()
@@ -494,7 +505,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["gemm", "attention", "f32gemm"],
+    ap.add_argument("--only", default=None, choices=["gemm", "attention", "f32gemm", "f32attn"],
                     help="run only this kernel's warm-up + timed launches (for ncu captures); prints no JSON")
     args = ap.parse_args()
     # Libraries (NCCL's version banner, ...) may write to fd 1; keep it for the one JSON line only.
