@@ -490,6 +490,11 @@ def extra_configs(args, lc, torch, dev, sp):
     gbs = 12.0 * n / (ms * 1e-3) / 1e9
     res["vector_add_f32_2^28"] = {"ms": ms, "gbs": gbs, "frac_of_hbm": gbs / hbm, "hbm_peak": f"{hbm} ({pk_kind})"}
     del va, vb, vc
+    # fp32 configs against both nominal ceilings (no measured fp32 / tf32 peak is available):
+    # CUDA-core fp32 = 148 SMs x 128 FMA/clk x 2 x 1.965 GHz; 3xTF32 = dense tf32 1125 / 3.
+    for key in [k for k in res if k.startswith(("cfg1", "cfg2", "cfg5"))]:
+        res[key]["frac_fp32_simt_nominal"] = res[key]["tflops"] / 74.4
+        res[key]["frac_3xtf32_nominal"] = res[key]["tflops"] / 375.0
     rows, cols = 65536, 1024
     x = torch.randn((rows, cols), device=dev)
     y = torch.empty_like(x)
