@@ -237,10 +237,23 @@ def run_ours(args, rank, world, local_rank):
                                                      C.c_void_p(fv.data_ptr()), C.c_void_p(fo.data_ptr()), 32, 3136,
                                                      64, 0, lc.F32, None, sp), "attention f32")
 
+    def cfg5_fn():
+        # The integrated conv -> QKV -> attention -> projection pipeline at the config-5 shape.
+        g.manual_seed(4)
+        x = torch.randn((32, 64, 56, 56), generator=g, device=dev)
+        w = (torch.rand((192, 64, 3, 3), generator=g, device=dev) * 2 - 1) * (6 / 576) ** 0.5
+        bias = torch.zeros(192, device=dev)
+        pw = (torch.rand((64, 64), generator=g, device=dev) * 2 - 1) * (6 / 64) ** 0.5
+        out = torch.empty((32, 3136, 64), device=dev)
+        return lambda: lc.check(L.lcConvAttentionNchw(C.c_void_p(x.data_ptr()), C.c_void_p(w.data_ptr()),
+                                                      C.c_void_p(bias.data_ptr()), C.c_void_p(pw.data_ptr()),
+                                                      C.c_void_p(out.data_ptr()), 32, 64, 56, 56, 192, 3, 3, 1, 1,
+                                                      1, 1, 3136, 64, 64, 1, None, sp), "conv attention")
+
     if args.only:
-        fn = {"gemm": gemm, "attention": attn, "f32gemm": None, "f32attn": None}[args.only]
+        fn = {"gemm": gemm, "attention": attn, "f32gemm": None, "f32attn": None, "cfg5": None}[args.only]
         if fn is None:
-            fn = f32gemm_fn() if args.only == "f32gemm" else f32attn_fn()
+            fn = {"f32gemm": f32gemm_fn, "f32attn": f32attn_fn, "cfg5": cfg5_fn}[args.only]()
         for _ in range(args.warmup + args.steps):
             fn()
         torch.cuda.synchronize()
@@ -510,7 +523,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--only", default=None, choices=["gemm", "attention", "f32gemm", "f32attn"],
+    ap.add_argument("--only", default=None, choices=["gemm", "attention", "f32gemm", "f32attn", "cfg5"],
                     help="run only this kernel's warm-up + timed launches (for ncu captures); prints no JSON")
     args = ap.parse_args()
     # Libraries (NCCL's version banner, ...) may write to fd 1; keep it for the one JSON line only.

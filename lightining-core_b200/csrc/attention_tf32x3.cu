@@ -114,16 +114,27 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 
 // ---- pre-pass -----------------------------------------------------------------------------------
 // Rows of 64 floats (unit u at src + u*unit_stride) -> contiguous hi/lo planes [units, S, 64].
+// blockIdx.y = unit; four floats per thread when the unit start is 16-byte aligned.
 __global__ void split_rows_kernel(const float* __restrict__ src, long long unit_stride, float* __restrict__ hi,
-                                  float* __restrict__ lo, int units, int seq) {
-  const long long total = static_cast<long long>(units) * seq * D;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long u = i / (static_cast<long long>(seq) * D);
-    const long long r = i - u * seq * D;
-    const float v = src[u * unit_stride + r];
-    const float h = tf32_round(v);
-    hi[i] = h;
-    lo[i] = v - h;
+                                  float* __restrict__ lo, int seq) {
+  const int u = blockIdx.y;
+  const float* su = src + static_cast<long long>(u) * unit_stride;
+  float* hu = hi + static_cast<long long>(u) * seq * D;
+  float* lu = lo + static_cast<long long>(u) * seq * D;
+  const int n = seq * D;
+  if ((reinterpret_cast<uintptr_t>(su) & 15u) == 0) {
+    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += gridDim.x * blockDim.x * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(su + i);
+      const float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+      *reinterpret_cast<float4*>(hu + i) = h;
+      *reinterpret_cast<float4*>(lu + i) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    }
+  } else {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+      const float v = su[i], h = tf32_round(v);
+      hu[i] = h;
+      lu[i] = v - h;
+    }
   }
 }
 // V [units][S][64] (unit stride) -> hi/lo planes of V^T [units][64][Sp], zero for keys >= S.
@@ -466,7 +477,7 @@ bool make_tmap_f32_3d(CUtensorMap* map, const void* base, int units, int rows, i
 bool attention_f32_tc_supported(const AttnArgs& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const int cols = a.proj_w ? a.proj_cols : a.d;
-  return a.d == D && a.lse == nullptr && a.seq >= 1 && cols >= 1 && cols <= 256 && al(a.out) &&
+  return a.d == D && a.lse == nullptr && a.seq >= 1 && a.seq <= (1 << 24) && cols >= 1 && cols <= 256 && al(a.out) &&
          (a.out_unit_stride % 4) == 0 && (cols % 4 == 0 || a.proj_w != nullptr) &&
          !(a.proj_w && a.post_relu) && tensor_map_encoder() != nullptr;
 }
@@ -512,9 +523,10 @@ cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
     attr_set = true;
   }
   if ((e = cudaStreamWaitEvent(s, ctx->attn_tf32_done, 0)) != cudaSuccess) return e;
-  const int blocks = static_cast<int>(std::min<size_t>(nqk / 256 + 1, 148 * 8));
-  split_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.units, a.seq);
-  split_rows_kernel<<<blocks, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.units, a.seq);
+  const dim3 sgrid(static_cast<unsigned>(std::min<long long>((static_cast<long long>(a.seq) * D / 4 + 255) / 256, 64)),
+                   static_cast<unsigned>(a.units));
+  split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.seq);
+  split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.seq);
   split_vt_kernel<<<dim3((sp + 31) / 32, D / 32, a.units), dim3(32, 8), 0, s>>>(static_cast<const float*>(a.v),
                                                                                 a.v_unit_stride, vh, vl, a.seq, sp);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;

@@ -98,27 +98,46 @@ __global__ void tf32_split_rows_pad_kernel(const float* __restrict__ src, float*
 
 // im2col of an NCHW input as the K-major B^T planes of the conv GEMM: row j = (image, oh, ow),
 // column kk = (c, kh, kw) (the OIHW weight order), zero outside the padded input and for kk >= k.
-__global__ void tf32_im2col_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
-                                         int rows, int k, int kp, int in_c, int in_h, int in_w, int kh, int kw, int sh,
-                                         int sw, int ph, int pw, int oh, int ow) {
-  const long long total = static_cast<long long>(rows) * kp;
-  const int pix = oh * ow;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int j = static_cast<int>(i / kp);
-    const int kk = static_cast<int>(i - static_cast<long long>(j) * kp);
-    float v = 0.0f;
+// A block takes IM2COL_ROWS rows; a shared table maps kk to its input offset (c, dy, dx) once, so
+// the inner loop has no division and consecutive threads store consecutive columns.
+constexpr int IM2COL_ROWS = 8;
+constexpr int IM2COL_MAX_KP = 8192;
+__global__ void __launch_bounds__(256) tf32_im2col_split_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                                                float* __restrict__ lo, int rows, int k, int kp,
+                                                                int in_c, int in_h, int in_w, int kh, int kw, int sh,
+                                                                int sw, int ph, int pw, int oh, int ow) {
+  __shared__ int tab[IM2COL_MAX_KP];  // (c << 16) | (dy << 8) | dx, or -1 for padding columns
+  for (int kk = threadIdx.x; kk < kp; kk += blockDim.x) {
     if (kk < k) {
+      const int c = kk / (kh * kw), r = kk - c * kh * kw, dy = r / kw;
+      tab[kk] = (c << 16) | (dy << 8) | (r - dy * kw);
+    } else {
+      tab[kk] = -1;
+    }
+  }
+  __syncthreads();
+  const int pix = oh * ow;
+  for (int j0 = blockIdx.x * IM2COL_ROWS; j0 < rows; j0 += gridDim.x * IM2COL_ROWS) {
+    for (int jr = 0; jr < IM2COL_ROWS && j0 + jr < rows; ++jr) {
+      const int j = j0 + jr;
       const int n = j / pix, pp = j - n * pix;
       const int y = pp / ow, xo = pp - y * ow;
-      const int c = kk / (kh * kw), r = kk - c * kh * kw;
-      const int dy = r / kw, dx = r - dy * kw;
-      const int iy = y * sh + dy - ph, ix = xo * sw + dx - pw;
-      if (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
-        v = x[((static_cast<long long>(n) * in_c + c) * in_h + iy) * in_w + ix];
+      const float* xn = x + static_cast<long long>(n) * in_c * in_h * in_w;
+      float* hrow = hi + static_cast<long long>(j) * kp;
+      float* lrow = lo + static_cast<long long>(j) * kp;
+      for (int kk = threadIdx.x; kk < kp; kk += blockDim.x) {
+        const int t = tab[kk];
+        float v = 0.0f;
+        if (t >= 0) {
+          const int iy = y * sh + ((t >> 8) & 0xff) - ph, ix = xo * sw + (t & 0xff) - pw;
+          if (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
+            v = __ldg(xn + (static_cast<long long>(t >> 16) * in_h + iy) * in_w + ix);
+        }
+        const float h = tf32_round(v);
+        hrow[kk] = h;
+        lrow[kk] = v - h;
+      }
     }
-    const float h = tf32_round(v);
-    hi[i] = h;
-    lo[i] = v - h;
   }
 }
 
@@ -520,8 +539,11 @@ cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* 
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
   tf32_split_rows_pad_kernel<<<grid_for(static_cast<long long>(na)), 256, 0, s>>>(w, a_hi, a_lo, out_c, k, kp);
-  tf32_im2col_split_kernel<<<grid_for(static_cast<long long>(nb)), 256, 0, s>>>(
-      x, b_hi, b_lo, static_cast<int>(rows), k, kp, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow);
+  {
+    const long long blocks = (rows + IM2COL_ROWS - 1) / IM2COL_ROWS;
+    tf32_im2col_split_kernel<<<static_cast<unsigned>(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(
+        x, b_hi, b_lo, static_cast<int>(rows), k, kp, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow);
+  }
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   const int pix = oh * ow;
   return launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, out_c, static_cast<int>(rows), kp,
@@ -535,7 +557,9 @@ cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, f
                             cudaStream_t s) {
   const long long oh = (in_h + 2 * ph - kh) / sh + 1, ow = (in_w + 2 * pw - kw) / sw + 1;
   const long long macs = static_cast<long long>(out_c) * batch * oh * ow * in_c * kh * kw;
-  if (macs >= (1LL << 28) && out_c >= 32 && tensor_map_encoder() != nullptr)
+  const long long kp = (static_cast<long long>(in_c) * kh * kw + 3) & ~3LL;
+  if (macs >= (1LL << 28) && out_c >= 32 && kp <= IM2COL_MAX_KP && kh < 256 && kw < 256 && in_c < 32768 &&
+      tensor_map_encoder() != nullptr)
     return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
   return conv2d_nchw_f32_simt(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
 }
