@@ -7,16 +7,17 @@
 // A pre-pass writes hi/lo planes of Q and K ([units, S, 64]) and of V transposed ([units, 64, Sp],
 // Sp = S rounded up to 4), so every MMA operand is K-major in shared memory.
 //
-// One CTA = one 128-row Q tile, one CTA per SM (192 KB of shared memory), 224 threads:
+// One CTA = one 128-row Q tile, one CTA per SM (192 KB of shared memory), 352 threads:
 //   warp 0      TMA: Q hi/lo once, K hi/lo tiles (64 keys) into a 2-stage ring freed by S_j;
 //               warp 6: V^T hi/lo tiles into a 2-stage ring freed by P.V_j.
 //   warp 1      MMA: S_j = Q K_j^T (3 x 8 tcgen05.mma.kind::tf32, M=128 N=64 K=8) into one of two
 //               TMEM score buffers; O_j = P_j V_j (3 x 8 MMAs with P read from TMEM) into one of
 //               two TMEM buffers, a fresh partial per tile.
-//   warps 2..5  softmax, one query row per thread: scores into registers, running max m (lazy:
+//   warps 2..5, 7..10  softmax, two warps per query row (32 score/output columns each, row maxima
+//               and sums swapped through shared memory): scores into registers, running max m (lazy:
 //               rescale only when it grows by more than 2^8), p = 2^(s*scale*log2e - m), l += p,
 //               P_hi over S_j's own columns and P_lo into its own buffer; then the previous
-//               tile's O partial is folded into 64 per-row fp32 registers, O = O*alpha + O_tile
+//               tile's O partial is folded into 32 per-thread fp32 registers, O = O*alpha + O_tile
 //               (round-to-nearest adds: the tensor core's long fp32 accumulations drift).  The
 //               epilogue divides by l, applies the optional projection out = O @ W (W [64, cols])
 //               and the postprocess, and writes fp32 rows.
@@ -41,7 +42,7 @@ namespace {
 constexpr int D = 64;
 constexpr int TILE = 128;
 constexpr int TK = 64;
-constexpr int NUM_THREADS = 224;
+constexpr int NUM_THREADS = 352;
 constexpr int QCH = TILE * 128;       // one [128 rows x 32 fp32] swizzled chunk = 16 KB
 constexpr int KCH = TK * 128;         // [64 keys x 32 fp32] = 8 KB
 constexpr int VCH = D * 128;          // [64 d-rows x 32 keys] = 8 KB
@@ -61,10 +62,14 @@ struct Tail {
   uint64_t q_full;
   uint64_t k_full[2], v_full[2];
   uint64_t s_full[2];   // S_j in TMEM (the S group's only commit)
-  uint64_t p_full[2];   // P_hi/P_lo of tile j in TMEM (4 warp arrivals)
+  uint64_t p_full[2];   // P_hi/P_lo of tile j in TMEM (8 warp arrivals)
   uint64_t o_full[2];   // the O partial of tile j in TMEM (the P.V group's only commit)
-  uint64_t o_free[2];   // the softmax warps have folded that partial (4 arrivals)
+  uint64_t o_free[2];   // the softmax warps have folded that partial (8 arrivals)
   uint64_t drain;
+  // Row statistics exchanged between the two column halves of the softmax warps, tagged with
+  // the tile index: [tile & 1][half][row] running maxima, and [half][row] final sums.
+  unsigned long long xmax[2][2][TILE];
+  unsigned long long xsum[2][TILE];
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -94,22 +99,6 @@ __device__ __forceinline__ float exp2_acc(float x) {
   float y;
   asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void umma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                             uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* err,
-                                          unsigned code) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, err, code) ? 1 : 0;
-  return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
 // ---- pre-pass -----------------------------------------------------------------------------------
@@ -189,19 +178,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&st->k_full[b], 1);
       mbar_init(&st->v_full[b], 1);
       mbar_init(&st->s_full[b], 1);
-      mbar_init(&st->p_full[b], 4);
+      mbar_init(&st->p_full[b], 8);
       mbar_init(&st->o_full[b], 1);
-      mbar_init(&st->o_free[b], 4);
+      mbar_init(&st->o_free[b], 8);
     }
     mbar_init(&st->drain, 1);
     st->abort_flag = 0;
     fence_barrier_init();
+    tma_prefetch_desc(&map_kh);
+    tma_prefetch_desc(&map_kl);
+    tma_prefetch_desc(&map_vh);
+    tma_prefetch_desc(&map_vl);
     mbar_arrive_expect_tx(&st->q_full, 2 * Q_PLANE);
     for (int c = 0; c < 2; ++c) {
       tma_load_3d(sQh + c * QCH, &map_qh, c * 32, q0, unit, &st->q_full);
       tma_load_3d(sQl + c * QCH, &map_ql, c * 32, q0, unit, &st->q_full);
     }
   }
+  for (int i = threadIdx.x; i < 2 * 2 * TILE; i += NUM_THREADS) (&st->xmax[0][0][0])[i] = ~0ull;
+  for (int i = threadIdx.x; i < 2 * TILE; i += NUM_THREADS) (&st->xsum[0][0])[i] = ~0ull;
   if (warp == 0) {
     tmem_alloc(&st->tmem_base, TMEM_COLS);
     tmem_relinquish();
@@ -224,6 +219,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
+        if (j + 2 < n_kv)  // warm L2 for the K tile that will take this slot next
+          for (int c = 0; c < 2; ++c) {
+            tma_prefetch_l2_3d(&map_kh, c * 32, (j + 2) * TK, unit);
+            tma_prefetch_l2_3d(&map_kl, c * 32, (j + 2) * TK, unit);
+          }
         // Slot s last held K_{j-2}; S_{j-2} (single commit: s_full[j&1]) must be done.  S_j needs
         // the load issued here, so the parity wait is unambiguous.
         if (j >= 2 && !mbar_wait_bounded(&st->s_full[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
@@ -249,6 +249,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       int issued = 0;
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
+        if (j + 2 < n_kv)
+          for (int c = 0; c < 2; ++c) {
+            tma_prefetch_l2_3d(&map_vh, (j + 2) * TK + c * 32, 0, unit);
+            tma_prefetch_l2_3d(&map_vl, (j + 2) * TK + c * 32, 0, unit);
+          }
         // Slot s last held V_{j-2}; P.V_{j-2} (single commit: o_full[j&1]) must be done.
         if (j >= 2 && !mbar_wait_bounded(&st->o_full[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
           ok = false;
@@ -265,13 +270,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) drain(&st->v_full[j & 1], (j >> 1) & 1);
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
-      bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
+    // ------------------------------------------------------------ MMA issue (whole warp, elected lane)
+    {
+      bool ok = warp_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait_bounded(&st->k_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) return false;
+        if (!warp_wait_bounded(&st->k_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) return false;
         tc_fence_after();
         const uint32_t d = tmem + S_COL + static_cast<uint32_t>(s * TK);
         const uint32_t qh = smem_u32(sQh), ql = smem_u32(sQl);
@@ -279,13 +284,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < D / 8; ++kk) {
           const uint32_t qo = (kk >> 2) * QCH + (kk & 3) * 32, ko = (kk >> 2) * KCH + (kk & 3) * 32;
-          umma_tf32_ss(d, smem_desc_sw128(ql + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC,
+          umma_tf32_ss_w(d, smem_desc_sw128(ql + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC,
                        kk > 0 ? 1u : 0u);
-          umma_tf32_ss(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kl + ko, 16, 1024), IDESC, 1u);
-          umma_tf32_ss(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC, 1u);
+          umma_tf32_ss_w(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kl + ko, 16, 1024), IDESC, 1u);
+          umma_tf32_ss_w(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC, 1u);
         }
         issued = true;
-        umma_commit(&st->s_full[s]);  // the only commit of this group
+        umma_commit_w(&st->s_full[s]);  // the only commit of this group
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -298,10 +303,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // p_full[s] next completes for P_{j+2}, which needs S_{j+2} (issued after this wait);
         // v_full[s] next completes after this P.V; o_free[s] next completes for the fold of
         // tile j, which needs this P.V.
-        if (!mbar_wait_bounded(&st->p_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !mbar_wait_bounded(&st->v_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+        if (!warp_wait_bounded(&st->p_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !warp_wait_bounded(&st->v_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
             (j >= 2 &&
-             !mbar_wait_bounded(&st->o_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait))) {
+             !warp_wait_bounded(&st->o_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait))) {
           ok = false;
           break;
         }
@@ -313,44 +318,66 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < TK / 8; ++kk) {
           const uint32_t vo = (kk >> 2) * VCH + (kk & 3) * 32;
-          umma_tf32_ts(o, pl + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
-          umma_tf32_ts(o, ph + kk * 8, smem_desc_sw128(vl + vo, 16, 1024), IDESC, 1u);
-          umma_tf32_ts(o, ph + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, 1u);
+          umma_tf32_ts_w(o, pl + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
+          umma_tf32_ts_w(o, ph + kk * 8, smem_desc_sw128(vl + vo, 16, 1024), IDESC, 1u);
+          umma_tf32_ts_w(o, ph + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, 1u);
         }
-        umma_commit(&st->o_full[s]);  // the only commit of this group
+        umma_commit_w(&st->o_full[s]);  // the only commit of this group
       }
       if (!ok && issued) {
-        umma_commit(&st->drain);
+        umma_commit_w(&st->drain);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
       }
     }
-  } else if (warp >= 2 && warp <= 5) {
+  } else if ((warp >= 2 && warp <= 5) || warp >= 7) {
     // ------------------------------------------------------------ softmax, fold, epilogue
+    // Two warps per TMEM lane quarter: half 0 (warps 2..5) owns score and output columns 0..31,
+    // half 1 (warps 7..10) columns 32..63 of the same rows.  The halves swap row maxima per tile
+    // (and sums at the end) through tagged shared-memory words.
     const int quarter = warp & 3;
+    const int half = warp >= 7 ? 1 : 0;
     const int row = quarter * 32 + lane;
     const int qrow = q0 + row;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t hc = static_cast<uint32_t>(half * 32);
     const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
     float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
-    float o_acc[D];
+    float o_acc[32];
 #pragma unroll
-    for (int e = 0; e < D; ++e) o_acc[e] = 0.0f;
+    for (int e = 0; e < 32; ++e) o_acc[e] = 0.0f;
     bool ok = true;
-    // Folds the O partial of tile t (in buffer t&1) into the registers: o = o * alpha + O_t.
+    // Publishes v under `tag` in `mine` and returns the partner's value under the same tag.
+    auto swap = [&](unsigned long long* mine, unsigned long long* theirs, uint32_t tag, float v, float* out) -> bool {
+      const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+      *reinterpret_cast<volatile unsigned long long*>(mine) = w;
+      volatile unsigned long long* t = theirs;
+      unsigned long long x = *t;
+      if (static_cast<uint32_t>(x >> 32) != tag) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (static_cast<uint32_t>((x = *t) >> 32) != tag) {
+          if (*abort_flag) return false;
+          if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > LC_WAIT_TIMEOUT_NS) {
+            *abort_flag = 1;
+            atomicCAS(p.err_word, 0u, static_cast<unsigned>(kErrAttnSoftmaxWait));
+            return false;
+          }
+        }
+      }
+      *out = __uint_as_float(static_cast<uint32_t>(x));
+      return true;
+    };
+    // Folds this half of the O partial of tile t (buffer t&1) into registers: o = o * alpha + O_t.
     auto fold = [&](int t, float alpha) -> bool {
       // o_full[t&1] next completes for P.V_{t+2}, which needs this fold's o_free first.
-      if (!warp_wait(&st->o_full[t & 1], (t >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) return false;
+      if (!warp_wait_bounded(&st->o_full[t & 1], (t >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) return false;
       tc_fence_after();
-      const uint32_t ob = tmem + lane_base + O_COL + static_cast<uint32_t>((t & 1) * D);
+      uint32_t r[32];
+      tmem_ld32(tmem + lane_base + O_COL + static_cast<uint32_t>((t & 1) * D) + hc, r);
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(ob + c, r);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) o_acc[c + e] = __fmaf_rn(o_acc[c + e], alpha, __uint_as_float(r[e]));
-      }
+      for (int e = 0; e < 32; ++e) o_acc[e] = __fmaf_rn(o_acc[e], alpha, __uint_as_float(r[e]));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&st->o_free[t & 1]);
@@ -359,53 +386,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
       // s_full[s] next completes for S_{j+2}, which needs P_j from these warps first.
-      if (!warp_wait(&st->s_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+      if (!warp_wait_bounded(&st->s_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const uint32_t sb = tmem + lane_base + S_COL + static_cast<uint32_t>(s * TK);
-      uint32_t r[TK];
-      {
-        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(r);
-        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(r + 32);
-        tmem_ld32(sb, r0);
-        tmem_ld32(sb + 32, r1);
-      }
-      const int kv0 = j * TK;
-      if (kv0 + TK - 1 > kmax) {
+      const uint32_t sb = tmem + lane_base + S_COL + static_cast<uint32_t>(s * TK) + hc;
+      uint32_t r[32];
+      tmem_ld32(sb, r);
+      const int kv0 = j * TK + half * 32;
+      if (kv0 + 31 > kmax) {
 #pragma unroll
-        for (int e = 0; e < TK; ++e)
+        for (int e = 0; e < 32; ++e)
           if (kv0 + e > kmax) r[e] = __float_as_uint(-INFINITY);
       }
-      float mx = __uint_as_float(r[0]);
+      float mx4[4];
 #pragma unroll
-      for (int e = 1; e < TK; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
-      mx *= p.scale_log2;
+      for (int i = 0; i < 4; ++i) mx4[i] = __uint_as_float(r[i]);
+#pragma unroll
+      for (int e = 4; e < 32; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], __uint_as_float(r[e]));
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), mo;
+      // Slot [j&1] is rewritten for tile j+2 only after the partner published tile j+1, which it
+      // does after reading this one.
+      if (!swap(&st->xmax[s][half][row], &st->xmax[s][half ^ 1][row], static_cast<uint32_t>(j), mx, &mo)) {
+        ok = false;
+        break;
+      }
+      mx = fmaxf(mx, mo) * p.scale_log2;
       float alpha = 1.0f;
       if (mx > m + RESCALE_THRESHOLD) {
         alpha = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
         l *= alpha;
         m = mx;
       }
-      // P_j: p = 2^(s*scale*log2e - m) in fp32; P_hi over S_j's columns, P_lo into its buffer.
-      // The last reader of both buffers before this was P.V_{j-2}, issued before S_j.
-      float lsum = 0.0f;
+      // P_j: p = 2^(s*scale*log2e - m) in fp32 (finite, <= 2^8); P_hi over S_j's columns, P_lo
+      // into its buffer.  The last reader of both buffers before this was P.V_{j-2}, issued
+      // before S_j.
+      float ls4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int g = 0; g < TK / 16; ++g) {
+      for (int g = 0; g < 2; ++g) {
         uint32_t wh[16], wl[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float pv = exp2_acc(__fmaf_rn(__uint_as_float(r[g * 16 + i]), p.scale_log2, -m));
-          const float ph = tf32_round(pv);
-          lsum += pv;
+          const float ph = __uint_as_float((__float_as_uint(pv) + 0x1000u) & 0xffffe000u);
+          ls4[i & 3] += pv;
           wh[i] = __float_as_uint(ph);
           wl[i] = __float_as_uint(pv - ph);
         }
         tmem_st16(sb + g * 16, wh);
-        tmem_st16(tmem + lane_base + PL_COL + static_cast<uint32_t>(s * TK + g * 16), wl);
+        tmem_st16(tmem + lane_base + PL_COL + static_cast<uint32_t>(s * TK) + hc + g * 16, wl);
       }
-      l += lsum;
+      l += (ls4[0] + ls4[1]) + (ls4[2] + ls4[3]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -418,19 +450,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       alpha_prev = alpha;
     }
-    if (ok && fold(n_kv - 1, alpha_prev) && qrow < p.seq) {
-      const float inv = 1.0f / l;
+    float lo_other = 0.0f;
+    if (ok && fold(n_kv - 1, alpha_prev) &&
+        swap(&st->xsum[half][row], &st->xsum[half ^ 1][row], static_cast<uint32_t>(n_kv), l, &lo_other) &&
+        qrow < p.seq) {
+      const float inv = 1.0f / (half == 0 ? l + lo_other : lo_other + l);
       float* orow = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(qrow) * p.cols;
       if (p.proj_w) {
-        for (int c = 0; c < p.cols; ++c) {
-          float acc = 0.0f;
+        // Both halves stage their normalised outputs in the (now idle) Q_hi buffer, rows padded
+        // to 65 floats, then each computes half of the projected columns over all 64 inputs.
+        float* ep = reinterpret_cast<float*>(sQh) + row * 65;
 #pragma unroll
-          for (int e = 0; e < D; ++e) acc = __fmaf_rn(o_acc[e] * inv, __ldg(p.proj_w + e * p.cols + c), acc);
-          orow[c] = acc;
+        for (int e = 0; e < 32; ++e) ep[half * 32 + e] = o_acc[e] * inv;
+        __threadfence_block();
+        // The ready flag reuses the max slots of tile n_kv, free by the same argument as a tile's.
+        float dummy;
+        const int fs = n_kv & 1;
+        if (swap(&st->xmax[fs][half][row], &st->xmax[fs][half ^ 1][row], static_cast<uint32_t>(n_kv), 0.0f, &dummy)) {
+          __threadfence_block();
+          const int c_mid = (p.cols + 1) / 2;
+          const int c_lo = half == 0 ? 0 : c_mid, c_hi = half == 0 ? c_mid : p.cols;
+          for (int c = c_lo; c < c_hi; ++c) {
+            float acc = 0.0f;
+#pragma unroll 16
+            for (int e = 0; e < D; ++e) acc = __fmaf_rn(ep[e], __ldg(p.proj_w + e * p.cols + c), acc);
+            orow[c] = acc;
+          }
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < D; e += 4) {
+        for (int e = 0; e < 32; e += 4) {
           float y[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
@@ -441,7 +490,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             y[i] = v;
           }
-          reinterpret_cast<float4*>(orow)[e / 4] = make_float4(y[0], y[1], y[2], y[3]);
+          reinterpret_cast<float4*>(orow + half * 32)[e / 4] = make_float4(y[0], y[1], y[2], y[3]);
         }
       }
     }
