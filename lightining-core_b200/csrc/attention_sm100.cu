@@ -328,7 +328,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(&st->s_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+      if (!warp_wait_poll(&st->s_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
         ok = false;
         break;
       }
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O is rescaled in place: PV_{j-1} must have landed first.
-        if (!warp_wait(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag, p.err_word,
+        if (!warp_wait_poll(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag, p.err_word,
                        kErrAttnCorrectionWait)) {
           ok = false;
           break;
@@ -425,9 +425,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     }
     // The last two PVs (one per P buffer) must have landed in O.
     if (ok && n_kv >= 2)
-      ok = warp_wait(&st->o_done[(n_kv - 2) % P_BUFS], ((n_kv - 2) >> 1) & 1, abort_flag, p.err_word,
+      ok = warp_wait_poll(&st->o_done[(n_kv - 2) % P_BUFS], ((n_kv - 2) >> 1) & 1, abort_flag, p.err_word,
                      kErrAttnCorrectionWait);
-    if (ok && warp_wait(&st->o_done[(n_kv - 1) % P_BUFS], ((n_kv - 1) >> 1) & 1, abort_flag, p.err_word,
+    if (ok && warp_wait_poll(&st->o_done[(n_kv - 1) % P_BUFS], ((n_kv - 1) >> 1) & 1, abort_flag, p.err_word,
                         kErrAttnCorrectionWait)) {
       tc_fence_after();
       // Epilogue: O / l (+ postprocess) as bf16 into the Q buffer, which no MMA reads any more
@@ -481,6 +481,381 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   }
 }
 
+// ---- two Q tiles per CTA, 128-key tiles (head_dim 128) -------------------------------------
+// One CTA per SM owns two 128-row Q tiles (A: rows q0..q0+127, B: q0+128..q0+255) of one unit,
+// which share every K/V tile.  KV tiles are 128 keys, so S = Q K^T runs as M=128 N=128 K=16
+// MMAs (operands 8 KB per MMA: the full tensor rate; 64-key tiles are bound by the 6 KB
+// shared-memory operand traffic of an N=64 MMA).  TMEM (all 512 columns): S_A 0, S_B 128,
+// O_A 256, O_B 384; P_h (bf16 pairs) overwrites the first 64 columns of S_h.  The MMA warp
+// alternates the tiles: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so each softmax warpgroup works on
+// its tile while the tensor core serves the other one.
+//   warp 0      TMA: Q_A, Q_B once, then K_j and V_j into 2-stage rings (freed by S_B(j) and
+//               PV_B(j), the last reader of each).
+//   warp 1      MMA issue (one thread).
+//   warps 2..5  softmax + epilogue of tile A; warps 6..9 of tile B.
+namespace q2 {
+constexpr int D = 128;
+constexpr int KT = 128;
+constexpr int NCH = 2;                       // 64-column chunks per 128-column row
+constexpr int CH = 128 * 128;                // one [128 rows x 64 bf16] swizzled box = 16 KB
+constexpr int TILE_BYTES = NCH * CH;         // 32 KB: a Q tile, a K tile or a V tile
+constexpr int Q_OFF = 0;                     // Q_A, Q_B
+constexpr int K_OFF = 2 * TILE_BYTES;        // 2 stages
+constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;
+constexpr int TAIL_OFF = V_OFF + 2 * TILE_BYTES;
+constexpr int THREADS = 320;
+struct Tail {
+  uint64_t q_full[2];
+  uint64_t k_full[2], v_full[2];
+  uint64_t k_free[2], v_free[2];  // stage free: S_B(j) / PV_B(j) done (one commit each)
+  uint64_t s_full[2];             // [tile]: S_h(j) in TMEM
+  uint64_t p_full[2];             // [tile]: P_h(j) in TMEM (4 warp arrivals)
+  uint64_t o_done[2];             // [tile]: PV_h(j) done
+  uint64_t o_staged[2];           // [tile]: bf16 O staged in Q_h (4 warp arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM = 1024 + TAIL_OFF + sizeof(Tail);
+}  // namespace q2
+
+__global__ void __launch_bounds__(q2::THREADS, 1)
+    fa2q_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                    const FaParams p) {
+  using namespace q2;
+  extern __shared__ __align__(16) uint8_t smem_raw2[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw2) + 1023) & ~uintptr_t(1023));
+  Tail* st = reinterpret_cast<Tail*>(smem + TAIL_OFF);
+  auto sQ = [&](int h) { return smem + Q_OFF + h * TILE_BYTES; };
+  auto sK = [&](int s) { return smem + K_OFF + s * TILE_BYTES; };
+  auto sV = [&](int s) { return smem + V_OFF + s * TILE_BYTES; };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nq2 = (p.seq + 2 * 128 - 1) / (2 * 128);
+  const int qt = nq2 - 1 - static_cast<int>(blockIdx.x) % nq2;  // heaviest tile pair first
+  const int unit = static_cast<int>(blockIdx.x) / nq2;
+  const int q0 = qt * 256;
+  const int kv_all = (p.seq + KT - 1) / KT;
+  int n_t[2];
+  n_t[0] = p.causal ? min(kv_all, (q0 + 127) / KT + 1) : kv_all;
+  n_t[1] = p.causal ? min(kv_all, (q0 + 255) / KT + 1) : kv_all;
+  const int nA = n_t[0], nB = n_t[1];  // nB >= nA
+
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&st->q_full[b], 1);
+      mbar_init(&st->k_full[b], 1);
+      mbar_init(&st->v_full[b], 1);
+      mbar_init(&st->k_free[b], 1);
+      mbar_init(&st->v_free[b], 1);
+      mbar_init(&st->s_full[b], 1);
+      mbar_init(&st->p_full[b], 4);
+      mbar_init(&st->o_done[b], 1);
+      mbar_init(&st->o_staged[b], 4);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+    tma_prefetch_desc(&map_o);
+    for (int h = 0; h < 2; ++h) {
+      mbar_arrive_expect_tx(&st->q_full[h], TILE_BYTES);
+      load_rows(sQ(h), &map_q, NCH, CH, q0 + h * 128, unit, &st->q_full[h]);
+    }
+  }
+  if (warp == 0) {
+    tmem_alloc(&st->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+  auto drain = [](uint64_t* bar, uint32_t ph) {
+    const uint64_t t1 = globaltimer_ns();
+    while (!mbar_try_wait(bar, ph) && globaltimer_ns() - t1 < 100000000ull) {
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer: K and V
+    if (lane == 0) {
+      bool ok = true;
+      int k_issued = 0, v_issued = 0;
+      for (int j = 0; j < nB && ok; ++j) {
+        const int s = j & 1;
+        // Stage s last held tile j-2, whose last readers are S_B(j-2) and PV_B(j-2); the next
+        // completion of k_free[s] / v_free[s] needs tile j, loaded here, so the waits are
+        // unambiguous.  PV_B(j-2) precedes S_B(j-1) in the MMA stream, so V never holds back K.
+        if (j >= 2 && !mbar_wait_bounded(&st->k_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&st->k_full[s], TILE_BYTES);
+        load_rows(sK(s), &map_k, NCH, CH, j * KT, unit, &st->k_full[s]);
+        ++k_issued;
+        if (j >= 2 && !mbar_wait_bounded(&st->v_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnLoadWait)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&st->v_full[s], TILE_BYTES);
+        load_rows(sV(s), &map_v, NCH, CH, j * KT, unit, &st->v_full[s]);
+        ++v_issued;
+        if (j + 2 < nB)
+          for (int c = 0; c < NCH; ++c) {
+            tma_prefetch_l2_3d(&map_k, c * 64, (j + 2) * KT, unit);
+            tma_prefetch_l2_3d(&map_v, c * 64, (j + 2) * KT, unit);
+          }
+      }
+      if (!ok) {
+        drain(&st->q_full[0], 0);
+        drain(&st->q_full[1], 0);
+        for (int j = k_issued > 2 ? k_issued - 2 : 0; j < k_issued; ++j) drain(&st->k_full[j & 1], (j >> 1) & 1);
+        for (int j = v_issued > 2 ? v_issued - 2 : 0; j < v_issued; ++j) drain(&st->v_full[j & 1], (j >> 1) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // The whole warp runs the issue loop and one elected lane issues each MMA, with the
+    // descriptors advanced by constant adds: beside eight busy softmax warps, a loop run by lane
+    // 0 alone issues several times slower.
+    {
+      constexpr uint32_t IDESC_S = idesc_bf16_f32(128, KT, 0, 0);  // Q K-major, K K-major
+      constexpr uint32_t IDESC_O = idesc_bf16_f32(128, D, 0, 1);   // P (TMEM) K-major, V MN-major
+      bool ok = true, issued = false;
+      auto wait = [&](uint64_t* bar, uint32_t ph) -> bool {
+        return warp_wait_poll(bar, ph, abort_flag, p.err_word, kErrAttnMmaWait);
+      };
+      auto issue_s = [&](int h, int j) {
+        const uint64_t qd = smem_desc_sw128(smem_u32(sQ(h)), 16, 1024);
+        const uint64_t kd = smem_desc_sw128(smem_u32(sK(j & 1)), 16, 1024);
+        const uint32_t d_tmem = tmem + static_cast<uint32_t>(h * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t o16 = ((kk >> 2) * CH + (kk & 3) * 32) >> 4;  // address field: bytes / 16
+          umma_f16_ss_w(d_tmem, qd + o16, kd + o16, IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit_w(&st->s_full[h]);
+      };
+      auto issue_pv = [&](int h, int j) {
+        const uint64_t vd = smem_desc_sw128(smem_u32(sV(j & 1)), CH, 1024);
+        const uint32_t o_tmem = tmem + 256 + static_cast<uint32_t>(h * 128);
+        const uint32_t a_tmem = tmem + static_cast<uint32_t>(h * 128);
+#pragma unroll
+        for (int kk = 0; kk < KT / 16; ++kk) {
+          // A = P_h in TMEM (2 keys per column, +8 columns per 16 keys); B = V MN-major, the two
+          // 64-column d chunks 16 KB apart (LBO), +16 key rows * 128 B per step.
+          umma_f16_ts_w(o_tmem, a_tmem + kk * 8, vd + (kk * 2048 >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit_w(&st->o_done[h]);
+      };
+      ok = wait(&st->q_full[0], 0) && wait(&st->k_full[0], 0);
+      if (ok) issue_s(0, 0);
+      if (ok) ok = wait(&st->q_full[1], 0);
+      if (ok) {
+        issue_s(1, 0);
+        umma_commit_w(&st->k_free[0]);
+      }
+      for (int j = 0; j < nB && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t par = (j >> 1) & 1;
+        // p_full[h] next completes for P_h(j+1), which needs S_h(j+1), issued after this wait.
+        if (!wait(&st->v_full[s], par)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (j < nA) {
+          if (!wait(&st->p_full[0], j & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j + 1 < nA) {
+            if (!wait(&st->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, j + 1);
+          }
+        }
+        if (!wait(&st->p_full[1], j & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit_w(&st->v_free[s]);
+        if (j + 1 < nB) {
+          if (!(j + 1 < nA) && !wait(&st->k_full[(j + 1) & 1], ((j + 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_s(1, j + 1);
+          umma_commit_w(&st->k_free[(j + 1) & 1]);
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_w(&st->drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue of tile h
+    const int h = warp >= 6 ? 1 : 0;
+    const int n = n_t[h];
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int qrow = q0 + h * 128 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>(h * 128);
+    const uint32_t o_tmem = tmem + lane_base + 256 + static_cast<uint32_t>(h * 128);
+    const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      // s_full[h] next completes for S_h(j+1), which needs P_h(j) from these warps first.
+      if (!warp_wait_poll(&st->s_full[h], j & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
+      tmem_wait_ld();
+      const int kv0 = j * KT;
+      if (kv0 + KT - 1 > kmax) {
+#pragma unroll
+        for (int e = 0; e < KT; ++e)
+          if (kv0 + e > kmax) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
+      }
+      float pm[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(r[0][a]);
+#pragma unroll
+      for (int e = 8; e < KT; e += 2)
+        pm[(e >> 1) & 7] = max3(pm[(e >> 1) & 7], __uint_as_float(r[e >> 5][e & 31]),
+                                __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31]));
+      const float mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
+                       p.scale_log2;
+      const bool need = mx > m + RESCALE_THRESHOLD;
+      float factor = 1.0f;
+      if (need) {
+        factor = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
+        l *= factor;
+        m = mx;
+      }
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O_h is rescaled in place: PV_h(j-1) must have landed (o_done[h] next completes for
+        // PV_h(j), which needs this tile's P).
+        if (!warp_wait_poll(&st->o_done[h], (j - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          uint32_t o[16];
+          tmem_ld16(o_tmem + c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+          tmem_st16(o_tmem + c, o);
+        }
+        tmem_wait_st();
+      }
+      // P_h(j) over the first 64 columns of S_h(j) (all of S_h(j) is in registers already).
+      const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
+      uint64_t ps2[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int g = 0; g < KT / 32; ++g) {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0, x1;
+          unpk2(fma2(pk2(__uint_as_float(r[g][2 * i]), __uint_as_float(r[g][2 * i + 1])), sc2, nm2), x0, x1);
+          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+          ps2[i & 3] = add2(ps2[i & 3], pk2(e0, e1));
+          w[i] = pack_bf16x2(e0, e1);
+        }
+        tmem_st16(s_tmem + g * 16, w);
+      }
+      {
+        const uint64_t t = add2(add2(ps2[0], ps2[1]), add2(ps2[2], ps2[3]));
+        float a, b;
+        unpk2(t, a, b);
+        l += a + b;
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->p_full[h]);
+    }
+    if (ok && warp_wait_poll(&st->o_done[h], (n - 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+      tc_fence_after();
+      // Epilogue: O / l (+ postprocess) as bf16 into Q_h (no MMA reads it any more: S_h(n-1)
+      // completed before PV_h(n-1)), 128-byte-swizzled, then TMA stores clipped at seq.
+      const float inv = 1.0f / l;
+      uint8_t* sq = sQ(h);
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + c, r);
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float y0 = __uint_as_float(r[2 * e]) * inv, y1 = __uint_as_float(r[2 * e + 1]) * inv;
+          if (p.post) {
+            y0 = y0 * p.post_scale + p.post_bias;
+            y1 = y1 * p.post_scale + p.post_bias;
+            if (p.post_relu) {
+              y0 = fmaxf(y0, 0.0f);
+              y1 = fmaxf(y1, 0.0f);
+            }
+          }
+          w[e] = pack_bf16x2(y0, y1);
+        }
+        uint8_t* srow = sq + (c >> 6) * CH + row * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int ch = ((c & 63) >> 3) + i;
+          *reinterpret_cast<uint4*>(srow + ((ch ^ (row & 7)) << 4)) =
+              make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&st->o_staged[h]);
+      // A tile wholly past the sequence end (short sequences) is never stored.
+      if ((warp & 3) == 2 && lane == 0 && q0 + h * 128 < p.seq &&
+          mbar_wait_bounded(&st->o_staged[h], 0, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+        for (int c = 0; c < NCH; ++c) tma_store_3d(&map_o, sq + c * CH, c * 64, q0 + h * 128, unit);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -496,6 +871,39 @@ bool make_tmap_heads(CUtensorMap* map, const void* base, int units, int seq, int
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+
+cudaError_t launch_fa2q(const AttnArgs& a, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, q2::D, 128) || !make_tmap_heads(&mk, a.k, a.units, a.seq, q2::D, 128) ||
+      !make_tmap_heads(&mv, a.v, a.units, a.seq, q2::D, 128) || !make_tmap_heads(&mo, a.out, a.units, a.seq, q2::D, 128))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;  // benign race: idempotent
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(fa2q_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(q2::SMEM));
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  FaParams p;
+  p.out = static_cast<__nv_bfloat16*>(a.out);
+  p.units = a.units;
+  p.seq = a.seq;
+  p.nq = (a.seq + 255) / 256;
+  p.causal = a.causal;
+  p.scale_log2 = a.scale * LOG2E;
+  p.post_scale = a.post_scale;
+  p.post_bias = a.post_bias;
+  p.post_relu = a.post_relu;
+  p.post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
+  p.err_word = ctx->err_word;
+  const long long blocks = static_cast<long long>(p.nq) * a.units;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  fa2q_fwd_kernel<<<static_cast<unsigned>(blocks), q2::THREADS, q2::SMEM, s>>>(mq, mk, mv, mo, p);
+  return cudaGetLastError();
 }
 
 template <int D>
@@ -547,7 +955,10 @@ cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) {
   std::string cfg;
   const bool forced_simt =
       tune_lookup(LC_TUNE_ATTENTION, a.seq, a.d, a.causal, LC_DTYPE_BF16, &cfg) && cfg == "simt";
-  if (!forced_simt && attention_bf16_tc_supported(a)) return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+  if (!forced_simt && attention_bf16_tc_supported(a)) {
+    if (a.d == 128 && cfg == kAttnTc2qName) return launch_fa2q(a, s);
+    return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+  }
   return attention_bf16_simt(a, s);
 }
 

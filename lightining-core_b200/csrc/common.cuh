@@ -211,6 +211,29 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+// Warp-wide bounded wait in which every lane polls (no divergent spin loop): cheaper to leave
+// than a lane-0 spin followed by a broadcast.  The verdict is made uniform with a vote.
+__device__ __forceinline__ bool warp_wait_poll(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               unsigned* err_word, unsigned code) {
+  bool ok = true;
+  if (!mbar_try_wait(bar, parity)) {
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, parity)) {
+      if (*abort_flag) {
+        ok = false;
+        break;
+      }
+      if ((++spins & 63u) == 0 && globaltimer_ns() - t0 > LC_WAIT_TIMEOUT_NS) {
+        *abort_flag = 1;
+        if (err_word) atomicCAS(err_word, 0u, code);
+        ok = false;
+        break;
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok);
+}
 // The same MMAs and commit issued from a converged warp: every lane executes the call and one
 // lane, chosen by elect.sync inside the asm, issues.  Keeping the whole warp on the issue path lets
 // the operands stay warp-uniform; a loop run by lane 0 alone issues slower.

@@ -108,6 +108,10 @@ cudaError_t attention_train_dv_update(const float* q, const float* k, float* v, 
 cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s);
 cudaError_t attention_bf16_simt(const AttnArgs& a, cudaStream_t s);
 bool attention_bf16_tc_supported(const AttnArgs& a);
+// The bf16 tensor-core kernels by their tune-cache names: one 128-row Q tile per CTA with 64-key
+// tiles (two CTAs per SM), and two Q tiles per CTA with 128-key tiles (head_dim 128).
+constexpr const char* kAttnTc1qName = "tcgen05_1q";
+constexpr const char* kAttnTc2qName = "tcgen05_2q";
 
 // ---- elementwise ----------------------------------------------------------------------------
 cudaError_t vector_add_f32(const float* a, const float* b, float* out, size_t n, cudaStream_t s);
