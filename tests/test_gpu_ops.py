@@ -69,6 +69,27 @@ def test_attention_bf16_shapes(gpu, units, s, d, causal):
     close_enough(ref, gpu.from_bf16(out), 2e-2, 2e-2)
 
 
+@pytest.mark.parametrize("kernel", ["tcgen05_1q", "tcgen05_2q"])
+@pytest.mark.parametrize("units,s,causal", [(1, 256, 0), (1, 256, 1), (2, 100, 1), (3, 777, 0), (2, 1000, 1),
+                                            (1, 300, 0), (1, 4100, 0)])
+def test_attention_bf16_each_tc_kernel(gpu, kernel, units, s, causal):
+    """Both bf16 tensor-core attention kernels for head_dim 128 (one Q tile per CTA with 64-key
+    tiles; two Q tiles per CTA with 128-key tiles), pinned through the tune cache, on ragged and
+    short sequences (a second Q tile wholly past the end included)."""
+    rng = np.random.default_rng(units * 31 + s + causal)
+    q, k, v = (P.bf16_round(rng.standard_normal((units, s, 128)).astype(np.float32)) for _ in range(3))
+    gpu.tune_cache_set(gpu.TUNE_ATTENTION, s, 128, causal, kernel, gpu.BF16)
+    try:
+        out = gpu.attention_batched(bf(gpu, q), bf(gpu, k), bf(gpu, v), bool(causal), gpu.BF16)
+    finally:
+        gpu.tune_cache_reset(gpu.TUNE_ATTENTION)
+    units_checked = range(units) if s <= 1000 else [0]
+    for u in units_checked:
+        rows = slice(0, s) if s <= 1000 else slice(s - 300, s)
+        ref = P.attention_rows(q[u], k[u], v[u], bool(causal), rows.start, rows.stop)
+        close_enough(ref, gpu.from_bf16(out)[u, rows], 2e-2, 2e-2)
+
+
 def test_attention_bf16_config3_sampled(gpu):
     """Config 3 at full size ([8,16,2048,128] causal), checked on sampled heads and rows."""
     rng = np.random.default_rng(2)
