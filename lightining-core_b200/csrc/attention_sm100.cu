@@ -281,28 +281,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (waits polled by every lane) and one elected lane issues
+    // each MMA, with descriptors advanced by constant adds.
+    {
       constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TK, 0, 0);    // Q K-major, K K-major
       constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P (TMEM) K-major, V MN-major
       const uint32_t q_addr = smem_u32(sQ);
-      bool ok = mbar_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
+      bool ok = warp_wait_poll(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
         const int s = j % K_STAGES;
-        if (!mbar_wait_bounded(&st->k_full[s], (j / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
+        if (!warp_wait_poll(&st->k_full[s], (j / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
           return false;
         tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + s * LY::KV_BYTES);
+        const uint64_t qd = smem_desc_sw128(q_addr, 16, 1024);
+        const uint64_t kd = smem_desc_sw128(smem_u32(sK + s * LY::KV_BYTES), 16, 1024);
         const uint32_t d_tmem = tmem + static_cast<uint32_t>((j & 1) * TK);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qoff = (kk >> 2) * CHUNK_BYTES + (kk & 3) * 32;
-          const uint32_t koff = (kk >> 2) * KCHUNK_BYTES + (kk & 3) * 32;
-          umma_f16_ss(d_tmem, smem_desc_sw128(q_addr + qoff, 16, 1024), smem_desc_sw128(k_addr + koff, 16, 1024),
-                      IDESC_S, kk > 0 ? 1u : 0u);
+          const uint32_t qo16 = ((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;  // address field: bytes / 16
+          const uint32_t ko16 = ((kk >> 2) * KCHUNK_BYTES + (kk & 3) * 32) >> 4;
+          umma_f16_ss_w(d_tmem, qd + qo16, kd + ko16, IDESC_S, kk > 0 ? 1u : 0u);
         }
         issued = true;
-        umma_commit(&st->s_full[j & 1]);  // the only commit of this MMA group
+        umma_commit_w(&st->s_full[j & 1]);  // the only commit of this MMA group
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -315,26 +317,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         // One barrier per TMEM buffer: p_full[j&1] next completes for P_{j+2}, which needs S_{j+2},
         // issued only after this wait, so the parity wait is unambiguous.  (A single barrier
         // waited with parity j&1 could already have completed P_j and P_{j+1}.)
-        if (!mbar_wait_bounded(&st->p_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !mbar_wait_bounded(&st->v_full[s], (j / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
+        if (!warp_wait_poll(&st->p_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !warp_wait_poll(&st->v_full[s], (j / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + s * LY::KV_BYTES);
+        const uint64_t vd = smem_desc_sw128(smem_u32(sV + s * LY::KV_BYTES), KCHUNK_BYTES, 1024);
         const uint32_t o_tmem = tmem + 2 * TK;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
           // A = P_j in TMEM (lanes = rows, 2 keys per column): +8 columns per 16 keys.  B = V,
           // MN-major: 64-column d chunks 8 KB apart (LBO), +16 key rows * 128 B per step.
           const uint32_t a_tmem = tmem + static_cast<uint32_t>((j % P_BUFS) * TK + kk * 8);
-          const uint64_t bdesc = smem_desc_sw128(v_addr + kk * 2048, KCHUNK_BYTES, 1024);
-          umma_f16_ts(o_tmem, a_tmem, bdesc, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts_w(o_tmem, a_tmem, vd + (kk * 2048 >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&st->o_done[j % P_BUFS]);  // the only commit of this MMA group
+        umma_commit_w(&st->o_done[j % P_BUFS]);  // the only commit of this MMA group
       }
       if (!ok && issued) {
-        umma_commit(&st->drain);
+        umma_commit_w(&st->drain);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
