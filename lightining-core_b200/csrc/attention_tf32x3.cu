@@ -272,22 +272,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issue (whole warp, elected lane)
     {
-      bool ok = warp_wait_bounded(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
+      bool ok = warp_wait_poll(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
       bool issued = false;
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
-        if (!warp_wait_bounded(&st->k_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) return false;
+        if (!warp_wait_poll(&st->k_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) return false;
         tc_fence_after();
         const uint32_t d = tmem + S_COL + static_cast<uint32_t>(s * TK);
-        const uint32_t qh = smem_u32(sQh), ql = smem_u32(sQl);
-        const uint32_t kh = smem_u32(sK(s, 0)), kl = smem_u32(sK(s, 1));
+        // Descriptors built once per tile and advanced by constant adds (address field: bytes / 16).
+        const uint64_t qh = smem_desc_sw128(smem_u32(sQh), 16, 1024), ql = smem_desc_sw128(smem_u32(sQl), 16, 1024);
+        const uint64_t kh = smem_desc_sw128(smem_u32(sK(s, 0)), 16, 1024);
+        const uint64_t kl = smem_desc_sw128(smem_u32(sK(s, 1)), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < D / 8; ++kk) {
-          const uint32_t qo = (kk >> 2) * QCH + (kk & 3) * 32, ko = (kk >> 2) * KCH + (kk & 3) * 32;
-          umma_tf32_ss_w(d, smem_desc_sw128(ql + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC,
-                       kk > 0 ? 1u : 0u);
-          umma_tf32_ss_w(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kl + ko, 16, 1024), IDESC, 1u);
-          umma_tf32_ss_w(d, smem_desc_sw128(qh + qo, 16, 1024), smem_desc_sw128(kh + ko, 16, 1024), IDESC, 1u);
+          const uint32_t qo = ((kk >> 2) * QCH + (kk & 3) * 32) >> 4, ko = ((kk >> 2) * KCH + (kk & 3) * 32) >> 4;
+          umma_tf32_ss_w(d, ql + qo, kh + ko, IDESC, kk > 0 ? 1u : 0u);
+          umma_tf32_ss_w(d, qh + qo, kl + ko, IDESC, 1u);
+          umma_tf32_ss_w(d, qh + qo, kh + ko, IDESC, 1u);
         }
         issued = true;
         umma_commit_w(&st->s_full[s]);  // the only commit of this group
@@ -303,10 +304,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // p_full[s] next completes for P_{j+2}, which needs S_{j+2} (issued after this wait);
         // v_full[s] next completes after this P.V; o_free[s] next completes for the fold of
         // tile j, which needs this P.V.
-        if (!warp_wait_bounded(&st->p_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !warp_wait_bounded(&st->v_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+        if (!warp_wait_poll(&st->p_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !warp_wait_poll(&st->v_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
             (j >= 2 &&
-             !warp_wait_bounded(&st->o_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait))) {
+             !warp_wait_poll(&st->o_free[s], ((j - 2) >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait))) {
           ok = false;
           break;
         }
@@ -314,13 +315,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t o = tmem + O_COL + static_cast<uint32_t>(s * D);
         const uint32_t ph = tmem + S_COL + static_cast<uint32_t>(s * TK);   // P_hi over S_j
         const uint32_t pl = tmem + PL_COL + static_cast<uint32_t>(s * TK);  // P_lo
-        const uint32_t vh = smem_u32(sV(s, 0)), vl = smem_u32(sV(s, 1));
+        const uint64_t vh = smem_desc_sw128(smem_u32(sV(s, 0)), 16, 1024);
+        const uint64_t vl = smem_desc_sw128(smem_u32(sV(s, 1)), 16, 1024);
 #pragma unroll
         for (int kk = 0; kk < TK / 8; ++kk) {
-          const uint32_t vo = (kk >> 2) * VCH + (kk & 3) * 32;
-          umma_tf32_ts_w(o, pl + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, kk > 0 ? 1u : 0u);
-          umma_tf32_ts_w(o, ph + kk * 8, smem_desc_sw128(vl + vo, 16, 1024), IDESC, 1u);
-          umma_tf32_ts_w(o, ph + kk * 8, smem_desc_sw128(vh + vo, 16, 1024), IDESC, 1u);
+          const uint32_t vo = ((kk >> 2) * VCH + (kk & 3) * 32) >> 4;
+          umma_tf32_ts_w(o, pl + kk * 8, vh + vo, IDESC, kk > 0 ? 1u : 0u);
+          umma_tf32_ts_w(o, ph + kk * 8, vl + vo, IDESC, 1u);
+          umma_tf32_ts_w(o, ph + kk * 8, vh + vo, IDESC, 1u);
         }
         umma_commit_w(&st->o_full[s]);  // the only commit of this group
       }
@@ -372,7 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // Folds this half of the O partial of tile t (buffer t&1) into registers: o = o * alpha + O_t.
     auto fold = [&](int t, float alpha) -> bool {
       // o_full[t&1] next completes for P.V_{t+2}, which needs this fold's o_free first.
-      if (!warp_wait_bounded(&st->o_full[t & 1], (t >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) return false;
+      if (!warp_wait_poll(&st->o_full[t & 1], (t >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait)) return false;
       tc_fence_after();
       uint32_t r[32];
       tmem_ld32(tmem + lane_base + O_COL + static_cast<uint32_t>((t & 1) * D) + hc, r);
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
       // s_full[s] next completes for S_{j+2}, which needs P_j from these warps first.
-      if (!warp_wait_bounded(&st->s_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+      if (!warp_wait_poll(&st->s_full[s], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
         ok = false;
         break;
       }
