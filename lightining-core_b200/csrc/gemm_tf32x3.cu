@@ -262,7 +262,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp runs the loop (waits polled by every lane), one elected lane issues each MMA,
+    // descriptors are advanced by constant adds: next to busy epilogue warps a loop run by lane 0
+    // alone issues several times slower.
+    {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -275,7 +278,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (kc == 0) {
             // Buffer acc was last committed ACC_BUFS chunks ago; tmem_empty[acc] next completes
             // only after the commit that follows this wait.
-            if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+            if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
               ok = false;
               break;
             }
@@ -283,35 +286,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
           }
           // full[stage] next completes for the stage's next use, loaded only after the commit below.
-          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+          if (!warp_wait_poll(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a_hi = smem_u32(smem + stage * STAGE_BYTES);
-          const uint32_t a_lo = a_hi + A_PLANE_BYTES;
-          const uint32_t b_hi = a_hi + 2 * A_PLANE_BYTES;
-          const uint32_t b_lo = b_hi + B_PLANE_BYTES;
+          const uint64_t ahd0 = smem_desc_sw128(a_hi, 16, 1024);
+          const uint64_t ald0 = smem_desc_sw128(a_hi + A_PLANE_BYTES, 16, 1024);
+          const uint64_t bhd0 = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES, 16, 1024);
+          const uint64_t bld0 = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES + B_PLANE_BYTES, 16, 1024);
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
-            // A and B^T: K-major SW128, rows 128 B apart, 8-row groups 1 KB apart; +32 B per K=8 step.
-            const uint64_t ahd = smem_desc_sw128(a_hi + k * 32, 16, 1024);
-            const uint64_t ald = smem_desc_sw128(a_lo + k * 32, 16, 1024);
-            const uint64_t bhd = smem_desc_sw128(b_hi + k * 32, 16, 1024);
-            const uint64_t bld = smem_desc_sw128(b_lo + k * 32, 16, 1024);
+            // A and B^T: K-major SW128, rows 128 B apart, 8-row groups 1 KB apart; +32 B per K=8
+            // step (+2 in the descriptor's address field, bytes / 16).
             const uint32_t first = (kc > 0 || k > 0) ? 1u : 0u;
-            umma_tf32_ss(d_tmem, ald, bhd, IDESC, first);  // small terms first
-            umma_tf32_ss(d_tmem, ahd, bld, IDESC, 1u);
-            umma_tf32_ss(d_tmem, ahd, bhd, IDESC, 1u);
+            umma_tf32_ss_w(d_tmem, ald0 + k * 2, bhd0 + k * 2, IDESC, first);  // small terms first
+            umma_tf32_ss_w(d_tmem, ahd0 + k * 2, bld0 + k * 2, IDESC, 1u);
+            umma_tf32_ss_w(d_tmem, ahd0 + k * 2, bhd0 + k * 2, IDESC, 1u);
             issued = true;
           }
-          umma_commit(&st->empty[stage]);
+          umma_commit_w(&st->empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
           if (kc == CHUNK_KB - 1 || kb == num_kb - 1) {
-            umma_commit(&st->tmem_full[acc]);
+            umma_commit_w(&st->tmem_full[acc]);
             if (++acc == ACC_BUFS) {
               acc = 0;
               acc_phase ^= 1u;
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
       }
       if (!ok && issued) {
-        umma_commit(&st->drain);
+        umma_commit_w(&st->drain);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
