@@ -146,7 +146,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // The whole warp runs the loop (waits polled by every lane), one elected lane issues.
+    {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -154,38 +155,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       bool issued = false;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+        if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+          if (!warp_wait_poll(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * B_STAGE_BYTES);
+          // A: K-major SW128, rows 128 B apart, 8-row groups 1024 B apart; +32 B per K=16 step.
+          // B: MN-major SW128, 64-column chunks 8 KB apart (LBO), 8-row K groups 1024 B apart
+          // (SBO); +16 rows * 128 B per K=16 step.  Steps are added to the address field (bytes / 16).
+          const uint64_t ad0 = smem_desc_sw128(smem_u32(smem_a + stage * A_STAGE_BYTES), 16, 1024);
+          const uint64_t bd0 = smem_desc_sw128(smem_u32(smem_b + stage * B_STAGE_BYTES), B_CHUNK_BYTES, 1024);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            // A: K-major SW128, rows 128 B apart, 8-row groups 1024 B apart; +32 B per K=16 step.
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            // B: MN-major SW128, 64-column chunks 8 KB apart (LBO), 8-row K groups 1024 B apart
-            // (SBO); +16 rows * 128 B per K=16 step.
-            const uint64_t bdesc = smem_desc_sw128(b_addr + k * 2048, B_CHUNK_BYTES, 1024);
-            umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_f16_ss_w(d_tmem, ad0 + k * 2, bd0 + k * 128, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
             issued = true;
           }
-          umma_commit(&st->empty[stage]);
+          umma_commit_w(&st->empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&st->tmem_full[acc]);
+        umma_commit_w(&st->tmem_full[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
@@ -193,7 +192,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (!ok && issued) {
         // Abort path: wait (bounded) for every MMA already issued before TMEM is released.
-        umma_commit(&st->drain);
+        umma_commit_w(&st->drain);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
@@ -388,7 +387,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader CTA only) ----------------
-    if (lane == 0 && leader) {
+    // The whole warp runs the loop (waits polled by every lane), one elected lane issues.
+    if (leader) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -396,7 +396,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       bool ok = true, issued = false;
       for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
         // tmem_empty[acc] next completes after this accumulator is committed again (below).
-        if (!mbar_wait_bounded(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+        if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
           ok = false;
           break;
         }
@@ -405,35 +405,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         for (int kb = 0; kb < num_kb; ++kb) {
           // full[stage] next completes for the stage's next use, whose loads wait on empty[stage],
           // committed only below.
-          if (!mbar_wait_bounded(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+          if (!warp_wait_poll(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem_a + stage * A_STAGE_BYTES);
-          const uint32_t b_addr = smem_u32(smem_b + stage * B_STAGE_BYTES);
+          const uint64_t ad0 = smem_desc_sw128(smem_u32(smem_a + stage * A_STAGE_BYTES), 16, 1024);
+          const uint64_t bd0 = smem_desc_sw128(smem_u32(smem_b + stage * B_STAGE_BYTES), B_CHUNK_BYTES, 1024);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t adesc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
-            const uint64_t bdesc = smem_desc_sw128(b_addr + k * 2048, B_CHUNK_BYTES, 1024);
-            umma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+            // +32 B (A) and +2 KB (B) per K=16 step: +2 and +128 in the address field (bytes / 16).
+            umma_f16_ss_pair_w(d_tmem, ad0 + k * 2, bd0 + k * 128, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
             issued = true;
           }
-          umma_commit_pair(&st->empty[stage], 0x3);
+          umma_commit_pair_w(&st->empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit_pair(&st->tmem_full[acc], 0x3);
+        umma_commit_pair_w(&st->tmem_full[acc], 0x3);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       if (!ok && issued) {
-        umma_commit_pair(&st->drain, 0x1);
+        umma_commit_pair_w(&st->drain, 0x1);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
         }
