@@ -410,7 +410,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])), mo;
       // Slot [j&1] is rewritten for tile j+2 only after the partner published tile j+1, which it
       // does after reading this one.
-      if (!swap(&st->xmax[s][half][row], &st->xmax[s][half ^ 1][row], static_cast<uint32_t>(j), mx, &mo)) {
+      // The verdict is made warp-uniform: the tcgen05 loads and waits below are warp-collective.
+      if (!__all_sync(0xffffffffu,
+                      swap(&st->xmax[s][half][row], &st->xmax[s][half ^ 1][row], static_cast<uint32_t>(j), mx, &mo))) {
         ok = false;
         break;
       }
@@ -453,47 +455,65 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       alpha_prev = alpha;
     }
     float lo_other = 0.0f;
-    if (ok && fold(n_kv - 1, alpha_prev) &&
-        swap(&st->xsum[half][row], &st->xsum[half ^ 1][row], static_cast<uint32_t>(n_kv), l, &lo_other) &&
-        qrow < p.seq) {
-      const float inv = 1.0f / (half == 0 ? l + lo_other : lo_other + l);
-      float* orow = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(qrow) * p.cols;
-      if (p.proj_w) {
-        // Both halves stage their normalised outputs in the (now idle) Q_hi buffer, rows padded
-        // to 65 floats, then each computes half of the projected columns over all 64 inputs.
-        float* ep = reinterpret_cast<float*>(sQh) + row * 65;
+    const bool fin = ok && fold(n_kv - 1, alpha_prev) &&
+                     swap(&st->xsum[half][row], &st->xsum[half ^ 1][row], static_cast<uint32_t>(n_kv), l, &lo_other);
+    const float inv = 1.0f / (half == 0 ? l + lo_other : lo_other + l);
+    if (p.proj_w) {
+      // Both halves stage their normalised outputs in the (now idle) Q_hi buffer, rows padded to
+      // 65 floats; once both halves of all 32 rows of this lane quarter are there, each of the
+      // two warps projects 16 of those rows with the lanes over output columns, so W is read
+      // and the output written in coalesced 128-byte lines.  out[r][c] = sum_e O[r][e] W[e][c]
+      // in e order.
+      float* ep_base = reinterpret_cast<float*>(sQh);
+      bool rdy = true;
+      if (fin && qrow < p.seq) {
+        float* ep = ep_base + row * 65;
 #pragma unroll
         for (int e = 0; e < 32; ++e) ep[half * 32 + e] = o_acc[e] * inv;
         __threadfence_block();
         // The ready flag reuses the max slots of tile n_kv, free by the same argument as a tile's.
         float dummy;
         const int fs = n_kv & 1;
-        if (swap(&st->xmax[fs][half][row], &st->xmax[fs][half ^ 1][row], static_cast<uint32_t>(n_kv), 0.0f, &dummy)) {
-          __threadfence_block();
-          const int c_mid = (p.cols + 1) / 2;
-          const int c_lo = half == 0 ? 0 : c_mid, c_hi = half == 0 ? c_mid : p.cols;
-          for (int c = c_lo; c < c_hi; ++c) {
-            float acc = 0.0f;
-#pragma unroll 16
-            for (int e = 0; e < D; ++e) acc = __fmaf_rn(ep[e], __ldg(p.proj_w + e * p.cols + c), acc);
-            orow[c] = acc;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          float y[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float v = o_acc[e + i] * inv;
-            if (p.post) {
-              v = v * p.post_scale + p.post_bias;
-              if (p.post_relu && v < 0.0f) v = 0.0f;
+        rdy = swap(&st->xmax[fs][half][row], &st->xmax[fs][half ^ 1][row], static_cast<uint32_t>(n_kv), 0.0f, &dummy);
+      }
+      if (__all_sync(0xffffffffu, fin && rdy)) {
+        __threadfence_block();
+        for (int rr = 0; rr < 16; ++rr) {
+          const int r = quarter * 32 + half * 16 + rr;
+          if (q0 + r >= p.seq) break;
+          const float* ep = ep_base + r * 65;
+          float* orow_r = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(q0 + r) * p.cols;
+          for (int c0 = 0; c0 < p.cols; c0 += 64) {
+            const int ca = c0 + lane, cb = c0 + 32 + lane;
+            const bool va = ca < p.cols, vb = cb < p.cols;
+            float acc_a = 0.0f, acc_b = 0.0f;
+#pragma unroll 8
+            for (int e = 0; e < D; ++e) {
+              const float o = ep[e];
+              const float* wr = p.proj_w + e * p.cols;
+              if (va) acc_a = __fmaf_rn(o, __ldg(wr + ca), acc_a);
+              if (vb) acc_b = __fmaf_rn(o, __ldg(wr + cb), acc_b);
             }
-            y[i] = v;
+            if (va) orow_r[ca] = acc_a;
+            if (vb) orow_r[cb] = acc_b;
           }
-          reinterpret_cast<float4*>(orow + half * 32)[e / 4] = make_float4(y[0], y[1], y[2], y[3]);
         }
+      }
+    } else if (fin && qrow < p.seq) {
+      float* orow = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(qrow) * p.cols;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float v = o_acc[e + i] * inv;
+          if (p.post) {
+            v = v * p.post_scale + p.post_bias;
+            if (p.post_relu && v < 0.0f) v = 0.0f;
+          }
+          y[i] = v;
+        }
+        reinterpret_cast<float4*>(orow + half * 32)[e / 4] = make_float4(y[0], y[1], y[2], y[3]);
       }
     }
   }
