@@ -98,8 +98,8 @@ __global__ void tf32_split_rows_pad_kernel(const float* __restrict__ src, float*
 
 // im2col of an NCHW input as the K-major B^T planes of the conv GEMM: row j = (image, oh, ow),
 // column kk = (c, kh, kw) (the OIHW weight order), zero outside the padded input and for kk >= k.
-// A block takes IM2COL_ROWS rows; a shared table maps kk to its input offset (c, dy, dx) once, so
-// the inner loop has no division and consecutive threads store consecutive columns.
+// A block takes IM2COL_ROWS rows at a time; a shared table maps kk to its input offset (c, dy, dx)
+// once, so the inner loop has no division, and consecutive threads store consecutive columns.
 constexpr int IM2COL_ROWS = 8;
 constexpr int IM2COL_MAX_KP = 8192;
 __global__ void __launch_bounds__(256) tf32_im2col_split_kernel(const float* __restrict__ x, float* __restrict__ hi,
@@ -118,24 +118,38 @@ __global__ void __launch_bounds__(256) tf32_im2col_split_kernel(const float* __r
   __syncthreads();
   const int pix = oh * ow;
   for (int j0 = blockIdx.x * IM2COL_ROWS; j0 < rows; j0 += gridDim.x * IM2COL_ROWS) {
-    for (int jr = 0; jr < IM2COL_ROWS && j0 + jr < rows; ++jr) {
-      const int j = j0 + jr;
+    // Per row of the group: its image base and top-left input coordinate (rows past the end get
+    // an empty window, so every load below is skipped for them).
+    const float* xr[IM2COL_ROWS];
+    int iy0[IM2COL_ROWS], ix0[IM2COL_ROWS];
+#pragma unroll
+    for (int jr = 0; jr < IM2COL_ROWS; ++jr) {
+      const int j = min(j0 + jr, rows - 1);
       const int n = j / pix, pp = j - n * pix;
       const int y = pp / ow, xo = pp - y * ow;
-      const float* xn = x + static_cast<long long>(n) * in_c * in_h * in_w;
-      float* hrow = hi + static_cast<long long>(j) * kp;
-      float* lrow = lo + static_cast<long long>(j) * kp;
-      for (int kk = threadIdx.x; kk < kp; kk += blockDim.x) {
-        const int t = tab[kk];
-        float v = 0.0f;
-        if (t >= 0) {
-          const int iy = y * sh + ((t >> 8) & 0xff) - ph, ix = xo * sw + (t & 0xff) - pw;
-          if (iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
-            v = __ldg(xn + (static_cast<long long>(t >> 16) * in_h + iy) * in_w + ix);
+      xr[jr] = x + static_cast<long long>(n) * in_c * in_h * in_w;
+      iy0[jr] = j0 + jr < rows ? y * sh - ph : -(1 << 20);
+      ix0[jr] = xo * sw - pw;
+    }
+    // kk outer, rows inner: the group's IM2COL_ROWS loads are independent and in flight together.
+    for (int kk = threadIdx.x; kk < kp; kk += blockDim.x) {
+      const int t = tab[kk];
+      const int c = t >> 16, dy = (t >> 8) & 0xff, dx = t & 0xff;
+      float v[IM2COL_ROWS];
+#pragma unroll
+      for (int jr = 0; jr < IM2COL_ROWS; ++jr) {
+        const int iy = iy0[jr] + dy, ix = ix0[jr] + dx;
+        v[jr] = (t >= 0 && iy >= 0 && iy < in_h && ix >= 0 && ix < in_w)
+                    ? __ldg(xr[jr] + (static_cast<long long>(c) * in_h + iy) * in_w + ix)
+                    : 0.0f;
+      }
+#pragma unroll
+      for (int jr = 0; jr < IM2COL_ROWS; ++jr) {
+        if (j0 + jr < rows) {
+          const float h = tf32_round(v[jr]);
+          hi[static_cast<long long>(j0 + jr) * kp + kk] = h;
+          lo[static_cast<long long>(j0 + jr) * kp + kk] = v[jr] - h;
         }
-        const float h = tf32_round(v);
-        hrow[kk] = h;
-        lrow[kk] = v - h;
       }
     }
   }
