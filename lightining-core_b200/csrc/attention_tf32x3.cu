@@ -459,12 +459,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                      swap(&st->xsum[half][row], &st->xsum[half ^ 1][row], static_cast<uint32_t>(n_kv), l, &lo_other);
     const float inv = 1.0f / (half == 0 ? l + lo_other : lo_other + l);
     if (p.proj_w) {
-      // Both halves stage their normalised outputs in the (now idle) Q_hi buffer, rows padded to
-      // 65 floats; once both halves of all 32 rows of this lane quarter are there, each of the
-      // two warps projects 16 of those rows with the lanes over output columns, so W is read
-      // and the output written in coalesced 128-byte lines.  out[r][c] = sum_e O[r][e] W[e][c]
-      // in e order.
+      // Both halves stage their normalised outputs in the (now idle) Q buffers, rows padded to
+      // 65 floats, and half of W ([64, cols], cols <= 128) each into this lane quarter's copy in
+      // the (now idle) K/V rings; once both halves of all 32 rows of the quarter are there, each
+      // of the two warps projects 16 of those rows with the lanes over output columns (W rows
+      // and output lines contiguous).  out[r][c] = sum_e O[r][e] W[e][c] in e order.
       float* ep_base = reinterpret_cast<float*>(sQh);
+      float* wsm = reinterpret_cast<float*>(smem + K_OFF) + quarter * (D * p.cols);
+      for (int e = half * 32; e < half * 32 + 32; ++e)
+        for (int c = lane; c < p.cols; c += 32) wsm[e * p.cols + c] = __ldg(p.proj_w + e * p.cols + c);
+      __threadfence_block();
       bool rdy = true;
       if (fin && qrow < p.seq) {
         float* ep = ep_base + row * 65;
@@ -478,24 +482,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       if (__all_sync(0xffffffffu, fin && rdy)) {
         __threadfence_block();
-        for (int rr = 0; rr < 16; ++rr) {
-          const int r = quarter * 32 + half * 16 + rr;
-          if (q0 + r >= p.seq) break;
-          const float* ep = ep_base + r * 65;
-          float* orow_r = p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(q0 + r) * p.cols;
+        // All 16 rows at once: each W element read from shared memory feeds 32 independent
+        // accumulator chains (16 rows x 2 columns per lane); every chain still sums e in order.
+        constexpr int RB = 16;
+        for (int rr = 0; rr < 16; rr += RB) {
+          const int r0 = quarter * 32 + half * 16 + rr;
+          if (q0 + r0 >= p.seq) break;
+          const float* ep0 = ep_base + r0 * 65;
           for (int c0 = 0; c0 < p.cols; c0 += 64) {
             const int ca = c0 + lane, cb = c0 + 32 + lane;
             const bool va = ca < p.cols, vb = cb < p.cols;
-            float acc_a = 0.0f, acc_b = 0.0f;
-#pragma unroll 8
+            const int cal = va ? ca : 0, cbl = vb ? cb : 0;  // clamped reads; results masked on store
+            float acc[RB][2];
+#pragma unroll
+            for (int i = 0; i < RB; ++i) acc[i][0] = acc[i][1] = 0.0f;
+#pragma unroll 4
             for (int e = 0; e < D; ++e) {
-              const float o = ep[e];
-              const float* wr = p.proj_w + e * p.cols;
-              if (va) acc_a = __fmaf_rn(o, __ldg(wr + ca), acc_a);
-              if (vb) acc_b = __fmaf_rn(o, __ldg(wr + cb), acc_b);
+              const float* wr = wsm + e * p.cols;
+              const float wa = wr[cal], wb = wr[cbl];
+#pragma unroll
+              for (int i = 0; i < RB; ++i) {
+                const float o = ep0[i * 65 + e];
+                acc[i][0] = __fmaf_rn(o, wa, acc[i][0]);
+                acc[i][1] = __fmaf_rn(o, wb, acc[i][1]);
+              }
             }
-            if (va) orow_r[ca] = acc_a;
-            if (vb) orow_r[cb] = acc_b;
+#pragma unroll
+            for (int i = 0; i < RB; ++i) {
+              if (q0 + r0 + i >= p.seq) break;
+              float* orow_r =
+                  p.out + static_cast<long long>(unit) * p.out_unit_stride + static_cast<long long>(q0 + r0 + i) * p.cols;
+              if (va) orow_r[ca] = acc[i][0];
+              if (vb) orow_r[cb] = acc[i][1];
+            }
           }
         }
       }
@@ -548,7 +567,9 @@ bool make_tmap_f32_3d(CUtensorMap* map, const void* base, int units, int rows, i
 bool attention_f32_tc_supported(const AttnArgs& a) {
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   const int cols = a.proj_w ? a.proj_cols : a.d;
-  return a.d == D && a.lse == nullptr && a.seq >= 1 && a.seq <= (1 << 24) && cols >= 1 && cols <= 256 && al(a.out) &&
+  // With a projection the epilogue stages W per lane quarter in the 128 KB of K/V rings: cols <= 128.
+  return a.d == D && a.lse == nullptr && a.seq >= 1 && a.seq <= (1 << 24) && cols >= 1 &&
+         cols <= (a.proj_w ? 128 : 256) && al(a.out) &&
          (a.out_unit_stride % 4) == 0 && (cols % 4 == 0 || a.proj_w != nullptr) &&
          !(a.proj_w && a.post_relu) && tensor_map_encoder() != nullptr;
 }
