@@ -332,7 +332,8 @@ lcError_t lcMatMulSessionRunBatch(lcMatMulSession_t s, const void* a, const void
 /* ---- per-shape auto-tune cache (src/ops/matmul_metal.mm:416-577, src/attention_metal.mm:184-336) */
 /* CSV `#lc_tune_cache,<matmul|attention>,2` + `#columns,...`; keys (m,k,n,dtype) for matmul and
  * (seq,head_dim,causal,dtype) for attention; values are sm_100a kernel configuration names
- * ("simt128x128", "simt128x64", "simt64x64", "tcgen05_128x256", "simt", "tcgen05").  A NULL path
+ * (matmul: "simt128x128", "simt128x64", "simt64x64", "tcgen05_128x256", "tcgen05_2sm_256x256",
+ * "tcgen05_3xtf32", "simt"; attention: "tcgen05_1q", "tcgen05_2q", "tcgen05_3xtf32", "simt").  A NULL path
  * means CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE, which is also loaded on first use and
  * rewritten whenever an entry is added.  Load rejects a file with an unknown header
  * (LC_NOT_SUPPORTED) and keeps the current rows. */
@@ -350,6 +351,12 @@ lcError_t lcTuneCacheSet(lcTuneKind kind, size_t d0, size_t d1, size_t d2, lcDat
  * fastest and writes its name to `best`.  Synchronizes `stream`. */
 lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, size_t k, size_t n, lcDataType dtype,
                            lcStream_t stream, char* best, size_t cap);
+/* The same for attention over device [units, seq, head_dim] q / k / v / out (the per-shape mode
+ * auto-tune of autoTuneForwardMode, src/attention_metal.mm:1316-1420): every kernel that can take
+ * the shape is timed and the fastest is stored under (seq, head_dim, causal, dtype). */
+lcError_t lcAttentionAutotune(const void* q, const void* k, const void* v, void* out, size_t units, size_t seq,
+                              size_t head_dim, int causal, lcDataType dtype, lcStream_t stream, char* best,
+                              size_t cap);
 
 /* ---- device error word: kernels' bounded waits record where they gave up ---------------- */
 /* Returns LC_DRIVER_ERROR and the recorded code if any kernel on the current device gave up a

@@ -29,6 +29,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <string>
+
 #include "../../include/lc_b200.h"
 #include "common.cuh"
 #include "lc_internal.hpp"
@@ -144,16 +146,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-
-// Warp-uniform bounded wait: lane 0 waits, the verdict is broadcast, so the warp stays
-// converged for the .sync.aligned tcgen05 loads that follow even on the abort path.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, unsigned* err,
-                                          unsigned code) {
-  int ok = 0;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, abort_flag, err, code) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  return ok != 0;
 }
 
 // 3-D TMA load: coordinates (d, row, unit).
@@ -981,6 +973,19 @@ bool attention_bf16_tc_supported(const AttnArgs& a) {
   return (a.d == 64 || a.d == 128) && a.proj_w == nullptr && a.q_unit_stride == hs && a.k_unit_stride == hs &&
          a.v_unit_stride == hs && a.out_unit_stride == hs && al(a.q) && al(a.k) && al(a.v) && al(a.out) &&
          tensor_map_encoder() != nullptr;
+}
+
+cudaError_t attention_bf16_by_name(const AttnArgs& a, const std::string& name, cudaStream_t s) {
+  if (name == kAttnTc2qName) {
+    if (!attention_bf16_tc_supported(a) || a.d != 128) return cudaErrorNotSupported;
+    return launch_fa2q(a, s);
+  }
+  if (name == kAttnTc1qName) {
+    if (!attention_bf16_tc_supported(a)) return cudaErrorNotSupported;
+    return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+  }
+  if (name == "simt") return attention_bf16_simt(a, s);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) {

@@ -112,6 +112,11 @@ bool attention_bf16_tc_supported(const AttnArgs& a);
 // tiles (two CTAs per SM), and two Q tiles per CTA with 128-key tiles (head_dim 128).
 constexpr const char* kAttnTc1qName = "tcgen05_1q";
 constexpr const char* kAttnTc2qName = "tcgen05_2q";
+// Strict fp32 attention on tcgen05 (3xTF32) by its tune-cache name.
+constexpr const char* kAttnTf32x3Name = "tcgen05_3xtf32";
+// Runs one bf16 attention kernel by its tune-cache name ("tcgen05_1q", "tcgen05_2q", "simt")
+// without consulting the cache; cudaErrorNotSupported when that kernel cannot take the shape.
+cudaError_t attention_bf16_by_name(const AttnArgs& a, const std::string& name, cudaStream_t s);
 
 // ---- elementwise ----------------------------------------------------------------------------
 cudaError_t vector_add_f32(const float* a, const float* b, float* out, size_t n, cudaStream_t s);

@@ -6,10 +6,12 @@
 // line; version 1 and 2 files load, a file with an unknown header is ignored as a whole; the file
 // path comes from CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE and is loaded on first use.
 // Keys here are (m, k, n, dtype) for matmul and (seq, head_dim, causal, dtype) for attention;
-// values are kernel configuration names ("simt128x128", "tcgen05_128x256", ...).
+// values are kernel configuration names ("simt128x128", "tcgen05_128x256", "tcgen05_2q", ...).
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -264,6 +266,81 @@ lcError_t lcMatMulAutotune(const void* a, const void* b, void* out, size_t m, si
   cudaEventDestroy(e1);
   if (st != LC_SUCCESS) return st;
   tune_store(LC_TUNE_MATMUL, m, k, n, dtype, best_name);
+  if (best && cap) std::snprintf(best, cap, "%s", best_name.c_str());
+  return LC_SUCCESS;
+}
+
+// Times every attention kernel that can run the shape on the caller's device buffers ([units,
+// seq, head_dim] each, contiguous; 1 warm-up + median of 5 CUDA-event samples), records the fastest
+// for (seq, head_dim, causal, dtype) and returns its name: the per-shape mode choice of the
+// reference's autoTuneForwardMode (src/attention_metal.mm:1316-1420), over sm_100a kernels.
+lcError_t lcAttentionAutotune(const void* q, const void* k, const void* v, void* out, size_t units, size_t seq,
+                              size_t head_dim, int causal, lcDataType dtype, lcStream_t stream, char* best,
+                              size_t cap) {
+  if (!q || !k || !v || !out || units == 0 || seq == 0 || head_dim == 0) return LC_INVALID_VALUE;
+  if (dtype != LC_DTYPE_F32 && dtype != LC_DTYPE_BF16) return LC_NOT_SUPPORTED;
+  if (units > 65535 || seq > (size_t)INT_MAX || head_dim > 256) return LC_NOT_SUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = a.out_unit_stride = static_cast<long long>(seq * head_dim);
+  a.units = static_cast<int>(units);
+  a.seq = static_cast<int>(seq);
+  a.d = static_cast<int>(head_dim);
+  a.causal = causal ? 1 : 0;
+  a.scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
+  a.post_scale = 1.0f;
+  a.post_bias = 0.0f;
+  std::vector<std::string> cands;
+  if (dtype == LC_DTYPE_F32) {
+    if (attention_f32_tc_supported(a)) cands.push_back(kAttnTf32x3Name);
+  } else if (attention_bf16_tc_supported(a)) {
+    cands.push_back(kAttnTc1qName);
+    if (head_dim == 128) cands.push_back(kAttnTc2qName);
+  }
+  cands.push_back("simt");
+  auto run = [&](const std::string& c) -> cudaError_t {
+    if (dtype == LC_DTYPE_F32) return c == kAttnTf32x3Name ? attention_f32_tc(a, s) : attention_f32_simt(a, s);
+    return attention_bf16_by_name(a, c, s);
+  };
+  cudaEvent_t e0, e1;
+  if (cudaEventCreate(&e0) != cudaSuccess) return LC_DRIVER_ERROR;
+  if (cudaEventCreate(&e1) != cudaSuccess) {
+    cudaEventDestroy(e0);
+    return LC_DRIVER_ERROR;
+  }
+  double best_ms = 1e30;
+  std::string best_name;
+  lcError_t st = LC_SUCCESS;
+  for (const std::string& c : cands) {
+    cudaError_t e = run(c);
+    std::vector<float> ms;
+    for (int rep = 0; rep < 5 && e == cudaSuccess; ++rep) {
+      cudaEventRecord(e0, s);
+      e = run(c);
+      cudaEventRecord(e1, s);
+      if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+      float t = 0.f;
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&t, e0, e1);
+      ms.push_back(t);
+    }
+    if (e != cudaSuccess) {
+      st = from_cuda(e);
+      break;
+    }
+    std::sort(ms.begin(), ms.end());
+    if (ms[ms.size() / 2] < best_ms) {
+      best_ms = ms[ms.size() / 2];
+      best_name = c;
+    }
+  }
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (st != LC_SUCCESS) return st;
+  tune_store(LC_TUNE_ATTENTION, seq, head_dim, causal ? 1 : 0, dtype, best_name);
   if (best && cap) std::snprintf(best, cap, "%s", best_name.c_str());
   return LC_SUCCESS;
 }

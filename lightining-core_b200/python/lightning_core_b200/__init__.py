@@ -104,6 +104,7 @@ _SIGS = {
     "lcTuneCacheGet": (_i, [_i, _sz, _sz, _sz, _i, C.c_char_p, _sz]),
     "lcTuneCacheSet": (_i, [_i, _sz, _sz, _sz, _i, C.c_char_p]),
     "lcMatMulAutotune": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, _vp, C.c_char_p, _sz]),
+    "lcAttentionAutotune": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, _vp, C.c_char_p, _sz]),
     "lcConvAttentionNchwNoAlloc": (_i, [_vp] * 5 + [_sz] * 14 + [_i, _vp]),
     "lcAttentionSessionCreate": (_i, [C.POINTER(_vp), _sz, _sz, _sz, _i, _i]),
     "lcAttentionSessionDestroy": (_i, [_vp]),
@@ -488,6 +489,16 @@ def matmul_autotune(a: "DeviceBuffer", b: "DeviceBuffer", out: "DeviceBuffer", m
                     dtype: int = F32) -> str:
     buf = C.create_string_buffer(64)
     check(lib.lcMatMulAutotune(a.ptr, b.ptr, out.ptr, m, k, n, dtype, None, buf, 64), "matmul_autotune")
+    return buf.value.decode()
+
+
+def attention_autotune(q: "DeviceBuffer", k: "DeviceBuffer", v: "DeviceBuffer", out: "DeviceBuffer", units: int,
+                       seq: int, head_dim: int, causal: bool = False, dtype: int = F32) -> str:
+    """Times every attention kernel that can take the shape on device [units, seq, head_dim]
+    buffers, stores the fastest in the attention tune cache and returns its name."""
+    buf = C.create_string_buffer(64)
+    check(lib.lcAttentionAutotune(q.ptr, k.ptr, v.ptr, out.ptr, units, seq, head_dim, int(causal), dtype, None, buf,
+                                  64), "attention_autotune")
     return buf.value.decode()
 
 

@@ -99,6 +99,12 @@ def test_invalid_arguments_rejected_before_gpu(lc):
     pol.output_relu = 1
     assert L.lcAttentionProjForward(x, x, x, x, x, 1, 4, 4, 4, 0, lc.F32, C.byref(pol), None) == lc.LC_NOT_SUPPORTED
     assert L.lcAttentionQkvProjForward(x, 0, x, x, 4, 4, 4, None, None) == lc.LC_INVALID_VALUE
+    # attention autotune: null buffers / zero sizes / unsupported dtype or size, before any launch
+    buf = C.create_string_buffer(64)
+    assert L.lcAttentionAutotune(None, x, x, x, 1, 4, 4, 0, lc.F32, None, buf, 64) == lc.LC_INVALID_VALUE
+    assert L.lcAttentionAutotune(x, x, x, x, 1, 0, 4, 0, lc.F32, None, buf, 64) == lc.LC_INVALID_VALUE
+    assert L.lcAttentionAutotune(x, x, x, x, 1, 4, 4, 0, 7, None, buf, 64) == lc.LC_NOT_SUPPORTED
+    assert L.lcAttentionAutotune(x, x, x, x, 1, 4, 512, 0, lc.F32, None, buf, 64) == lc.LC_NOT_SUPPORTED
 
 
 def test_policy_defaults_and_loop_presets(lc):

@@ -95,3 +95,36 @@ def test_autotune_records_and_is_used(gpu, dtype, tmp_path, monkeypatch):
     got = out if dt == gpu.F32 else gpu.from_bf16(out)
     ref = O.port().matmul(a[:64], b, threads=8)
     close_enough(ref, got[:64], *((1e-4, 1e-4) if dt == gpu.F32 else (2e-3, 2e-2)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,d,causal", [("bf16", 128, 0), ("bf16", 128, 1), ("bf16", 64, 1), ("f32", 64, 0)])
+def test_attention_autotune_records_and_is_used(gpu, dtype, d, causal):
+    """lcAttentionAutotune times the kernels that can take the shape, stores the fastest under
+    (seq, head_dim, causal, dtype), and the next call through the dispatch uses it correctly."""
+    from oracle import oracle as O
+
+    units, seq = 4, 384
+    dt = gpu.F32 if dtype == "f32" else gpu.BF16
+    rng = np.random.default_rng(d + causal)
+    q, k, v = (rng.standard_normal((units, seq, d)).astype(np.float32) for _ in range(3))
+    if dt == gpu.BF16:
+        q, k, v = (O.port().bf16_round(x) for x in (q, k, v))
+        hq, hk, hv = (gpu.to_bf16(x) for x in (q, k, v))
+    else:
+        hq, hk, hv = q, k, v
+    dq, dk, dv = (gpu.DeviceBuffer.from_array(x) for x in (hq, hk, hv))
+    dout = gpu.DeviceBuffer(units * seq * d * (4 if dt == gpu.F32 else 2))
+    try:
+        best = gpu.attention_autotune(dq, dk, dv, dout, units, seq, d, bool(causal), dt)
+        allowed = {"simt", "tcgen05_3xtf32"} if dt == gpu.F32 else {"simt", "tcgen05_1q", "tcgen05_2q"}
+        assert best in allowed
+        assert best != "tcgen05_2q" or d == 128
+        assert gpu.tune_cache_get(gpu.TUNE_ATTENTION, seq, d, causal, dt) == best
+        out = gpu.attention_batched(hq, hk, hv, bool(causal), dt)
+    finally:
+        gpu.tune_cache_reset(gpu.TUNE_ATTENTION)
+    got = out if dt == gpu.F32 else gpu.from_bf16(out)
+    tol = (1e-4, 1e-4) if dt == gpu.F32 else (2e-2, 2e-2)
+    for u in range(units):
+        close_enough(O.port().attention(q[u], k[u], v[u], bool(causal)), got[u], *tol)
