@@ -72,7 +72,7 @@ class Clocks:
     """SM clock and throttle reasons sampled during the timed region.
 
     Polls NVML every 10 ms from a thread (reading only; nothing is set), so even a short timed
-    region gets samples; falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
+    region gets samples.  Without NVML the summary says "no samples"."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4}

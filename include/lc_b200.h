@@ -158,7 +158,7 @@ const char* lcGetErrorString(lcError_t error);
 /* ===================== Part 2: hot-path op entry points (new in this build) =============== */
 
 typedef enum lcDataType {
-  LC_DTYPE_F32 = 0,  /* fp32 in/out, strict fp32 arithmetic (SIMT FFMA)              */
+  LC_DTYPE_F32 = 0,  /* fp32 in/out, fp32-accurate: 3xTF32 on tcgen05, SIMT FFMA for small shapes */
   LC_DTYPE_BF16 = 1, /* bf16 in/out, fp32 accumulate/softmax on tcgen05 tensor cores */
   LC_DTYPE_F64 = 2   /* vector add only                                             */
 } lcDataType;

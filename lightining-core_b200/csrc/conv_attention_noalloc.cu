@@ -68,6 +68,8 @@ extern "C" lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, 
     return LC_INVALID_VALUE;
   if (head_dim > 256 || (proj_w && (head_dim > 128 || proj_cols > 128)) || seq > (size_t)INT_MAX)
     return LC_NOT_SUPPORTED;
+  if (!conv_dims_fit_int(in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w))
+    return LC_NOT_SUPPORTED;
   const size_t oh = (in_h + 2 * pad_h - kernel_h) / stride_h + 1;
   const size_t ow = (in_w + 2 * pad_w - kernel_w) / stride_w + 1;
   if (batch * oh * ow > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
@@ -85,6 +87,9 @@ extern "C" lcError_t lcConvAttentionNchwNoAlloc(const float* x, const float* w, 
   cudaError_t e = scratch_for_current_device(&scratch);
   if (e != cudaSuccess) return from_cuda(e);
   float* conv = scratch;
+  // The SIMT conv sizes its tile from cudaDeviceGetAttribute; it never creates the per-device
+  // library context (whose error word is allocated), so this path allocates nothing even as the
+  // first library call on a device.
   e = conv2d_nchw_f32_simt(x, w, bias, conv, (int)batch, (int)in_channels, (int)in_h, (int)in_w, (int)out_channels,
                       (int)kernel_h, (int)kernel_w, (int)stride_h, (int)stride_w, (int)pad_h, (int)pad_w, 1, s);
   if (e != cudaSuccess) return from_cuda(e);

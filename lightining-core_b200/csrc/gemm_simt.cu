@@ -184,9 +184,14 @@ enum SimtTile { kSimt128x128 = 0, kSimt128x64, kSimt64x64, kSimtTileCount };
 const char* const kSimtTileNames[kSimtTileCount] = {"simt128x128", "simt128x64", "simt64x64"};
 
 // Without a cache entry: the largest tile that still gives every SM a CTA.
+// Reads the SM count straight from the runtime (no DeviceCtx): the no-alloc pipeline runs this
+// conv and must not create the per-device context, whose error word is a cudaMalloc.
 int default_simt_tile(int M, int N) {
-  const DeviceCtx* c = device_ctx();
-  const long long sms = c ? c->sm_count : 148;
+  int dev = 0, sm_count = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sm_count <= 0)
+    sm_count = 148;
+  const long long sms = sm_count;
   const long long big = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
   if (big >= sms) return kSimt128x128;
   const long long mid = static_cast<long long>((M + 127) / 128) * ((N + 63) / 64);

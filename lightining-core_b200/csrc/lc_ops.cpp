@@ -519,7 +519,9 @@ lcError_t lcConv2dNchw(const float* x, const float* w, const float* bias, float*
     return LC_INVALID_VALUE;
   const size_t oh = (in_h + 2 * pad_h - kernel_h) / stride_h + 1;
   const size_t ow = (in_w + 2 * pad_w - kernel_w) / stride_w + 1;
-  if (batch * oh * ow > (size_t)INT_MAX || in_channels * kernel_h * kernel_w > (size_t)INT_MAX) return LC_NOT_SUPPORTED;
+  if (!conv_dims_fit_int(in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w) ||
+      batch * oh * ow > (size_t)INT_MAX)
+    return LC_NOT_SUPPORTED;
   lcConv2dIoPolicy pol = {0, 0, 0, 0, 0};
   if (policy) pol = *policy;
   Io io(static_cast<cudaStream_t>(stream));
@@ -549,6 +551,8 @@ lcError_t lcConvAttentionNchw(const float* x, const float* w, const float* bias,
       seq == 0 || head_dim == 0 || (proj_w && proj_cols == 0))
     return LC_INVALID_VALUE;
   if (head_dim > 256 || (proj_w && (head_dim > 128 || proj_cols > 128)) || seq > (size_t)INT_MAX)
+    return LC_NOT_SUPPORTED;
+  if (!conv_dims_fit_int(in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w, pad_h, pad_w))
     return LC_NOT_SUPPORTED;
   const size_t oh = (in_h + 2 * pad_h - kernel_h) / stride_h + 1;
   const size_t ow = (in_w + 2 * pad_w - kernel_w) / stride_w + 1;
