@@ -358,6 +358,52 @@ lcError_t lcAttentionAutotune(const void* q, const void* k, const void* v, void*
                               size_t head_dim, int causal, lcDataType dtype, lcStream_t stream, char* best,
                               size_t cap);
 
+/* ---- multi-GPU: one process per GPU, NCCL over NVLink -----------------------------------
+ * No counterpart in the reference, which runs on one device and has no collective (its batched
+ * workloads are independent units: attention heads, matmul rows, conv->attention images).  These
+ * shard those units across the ranks of a communicator and assemble the full output on every
+ * rank with one in-place NCCL all-gather (grouped broadcasts when units do not divide evenly).
+ * NCCL is loaded at run time (dlopen "libnccl.so.2"); lcCommAvailable() says whether it was found.
+ * A communicator belongs to the device that was current at lcCommInitRank; call it with that
+ * device current.  Shards are contiguous and balanced: rank r owns [lo, hi) of lcShardRange. */
+typedef struct lcComm* lcComm_t;
+typedef struct lcCommUniqueId { char internal[128]; } lcCommUniqueId; /* ncclUniqueId bytes */
+int lcCommAvailable(void);
+/* Rank 0 creates the id and hands it to the other ranks by any host channel. */
+lcError_t lcCommGetUniqueId(lcCommUniqueId* id);
+/* Collective over the nranks processes (ncclCommInitRank); binds the current device. */
+lcError_t lcCommInitRank(lcComm_t* comm, int nranks, const lcCommUniqueId* id, int rank);
+lcError_t lcCommDestroy(lcComm_t comm);
+/* Tears the communicator down without waiting for peers (ncclCommAbort): the way out after a
+ * peer failed. */
+lcError_t lcCommAbort(lcComm_t comm);
+lcError_t lcCommRankInfo(lcComm_t comm, int* rank, int* nranks);
+lcError_t lcShardRange(size_t total, int rank, int nranks, size_t* lo, size_t* hi);
+/* In-place all-gather of total_rows rows of row_bytes: this rank's rows [lo, hi) are in place in
+ * the device buffer `buf`; on return (stream order) every rank holds all rows. */
+lcError_t lcCommAllGatherRows(lcComm_t comm, void* buf, size_t total_rows, size_t row_bytes, lcStream_t stream);
+/* lcAttentionForward / lcMatMul / lcConvAttentionNchw (per_image = 1) over a communicator.
+ * Arguments describe the FULL problem, identical on every rank; each rank computes its shard of
+ * units / rows of A / images.  Policies keep their single-GPU meaning per pointer:
+ *   - device output (download_out = 0): after the call every rank holds the full output;
+ *   - host output (download_out = 1): each rank downloads only its own rows into `out`
+ *     (no gather: the host buffers of the ranks are separate);
+ *   - host inputs are uploaded per shard; the matmul's replicated B (upload_b = 1) is uploaded as a
+ *     1/N row slice per rank and all-gathered over NVLink into a buffer the communicator owns.
+ * synchronize (or a host output) waits for the stream and reports NCCL's asynchronous errors and
+ * the device error word. */
+lcError_t lcAttentionForwardSharded(lcComm_t comm, const void* q, const void* k, const void* v, void* out,
+                                    size_t units, size_t seq, size_t head_dim, int causal, lcDataType dtype,
+                                    const lcAttentionIoPolicy* policy, lcStream_t stream);
+lcError_t lcMatMulSharded(lcComm_t comm, const void* a, const void* b, void* out, size_t m, size_t k, size_t n,
+                          lcDataType dtype, const lcMatMulIoPolicy* policy, lcStream_t stream);
+lcError_t lcConvAttentionNchwSharded(lcComm_t comm, const float* x, const float* w, const float* bias,
+                                     const float* proj_w, float* out, size_t batch, size_t in_channels, size_t in_h,
+                                     size_t in_w, size_t out_channels, size_t kernel_h, size_t kernel_w,
+                                     size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w, size_t seq,
+                                     size_t head_dim, size_t proj_cols, const lcConv2dIoPolicy* policy,
+                                     lcStream_t stream);
+
 /* ---- device error word: kernels' bounded waits record where they gave up ---------------- */
 /* Returns LC_DRIVER_ERROR and the recorded code if any kernel on the current device gave up a
  * bounded wait since the last clear; LC_SUCCESS otherwise.  Synchronizes the device. */

@@ -118,6 +118,17 @@ _SIGS = {
     "lcMatMulSessionRunBatch": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "lcAttentionTrainStep": (_i, [_vp] * 5 + [_f, _sz, _sz, _sz, _i, _vp, C.POINTER(AttentionIoPolicy), _vp]),
     "lcAttentionSessionTrainStep": (_i, [_vp] * 6 + [_f, _vp, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcCommAvailable": (_i, []),
+    "lcCommGetUniqueId": (_i, [_vp]),
+    "lcCommInitRank": (_i, [C.POINTER(_vp), _i, _vp, _i]),
+    "lcCommDestroy": (_i, [_vp]),
+    "lcCommAbort": (_i, [_vp]),
+    "lcCommRankInfo": (_i, [_vp, C.POINTER(_i), C.POINTER(_i)]),
+    "lcShardRange": (_i, [_sz, _i, _i, C.POINTER(_sz), C.POINTER(_sz)]),
+    "lcCommAllGatherRows": (_i, [_vp, _vp, _sz, _sz, _vp]),
+    "lcAttentionForwardSharded": (_i, [_vp] * 5 + [_sz, _sz, _sz, _i, _i, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcMatMulSharded": (_i, [_vp] * 4 + [_sz, _sz, _sz, _i, C.POINTER(MatMulIoPolicy), _vp]),
+    "lcConvAttentionNchwSharded": (_i, [_vp] * 6 + [_sz] * 14 + [C.POINTER(Conv2dIoPolicy), _vp]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -626,3 +637,40 @@ def attention_train_step(q, k, v, target, learning_rate: float, causal: bool = F
     check(lib.lcAttentionTrainStep(_vp(q), _vp(k), _vp(v), _vp(t), _vp(out), learning_rate, units, seq, d,
                                    int(causal), _vp(loss), C.byref(pol), None), "attention_train_step")
     return out, v, (float(loss[0]) if q.ndim == 2 else loss)
+
+
+# ---- multi-GPU (one process per GPU) -----------------------------------------------------------
+class Comm:
+    """A communicator of liblc_b200.so (NCCL underneath) for this process's current device.
+
+    `exchange(bytes) -> bytes` hands rank 0's 128-byte unique id to every rank over whatever host
+    channel the caller already has (e.g. a torch.distributed broadcast); it is called on every rank
+    with rank 0's id (other ranks pass zeros) and must return rank 0's bytes."""
+
+    def __init__(self, rank: int, nranks: int, exchange):
+        if not lib.lcCommAvailable():
+            raise RuntimeError("NCCL (libnccl.so.2) could not be loaded")
+        uid = (C.c_char * 128)()
+        if rank == 0:
+            check(lib.lcCommGetUniqueId(uid), "lcCommGetUniqueId")
+        got = exchange(bytes(uid))
+        if len(got) != 128:
+            raise ValueError("unique id must be 128 bytes")
+        uid = (C.c_char * 128).from_buffer_copy(got)
+        self.handle = C.c_void_p()
+        check(lib.lcCommInitRank(C.byref(self.handle), nranks, uid, rank), "lcCommInitRank")
+        self.rank, self.nranks = rank, nranks
+
+    def close(self, abort: bool = False) -> None:
+        if self.handle:
+            fn = lib.lcCommAbort if abort else lib.lcCommDestroy
+            check(fn(self.handle), "lcCommAbort" if abort else "lcCommDestroy")
+            self.handle = C.c_void_p()
+
+
+def shard_range(total: int, rank: int, nranks: int) -> tuple[int, int]:
+    """[lo, hi) of `total` units owned by `rank` (the library's balanced contiguous split)."""
+    lo, hi = C.c_size_t(), C.c_size_t()
+    if lib.lcShardRange(total, rank, nranks, C.byref(lo), C.byref(hi)) != LC_SUCCESS:
+        raise ValueError("bad shard request")
+    return lo.value, hi.value

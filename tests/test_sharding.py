@@ -78,3 +78,55 @@ def test_gloo_sharded_step_matches_unsharded(tmp_path, world):
     for r in range(world):
         np.testing.assert_array_equal(np.load(tmp_path / f"att_{r}.npy"), want_att)
         np.testing.assert_array_equal(np.load(tmp_path / f"c_{r}.npy"), want_c)
+
+
+def test_library_shard_range_matches(lc):
+    """lcShardRange (the split the library's sharded entry points use) == the harness split."""
+    for total in (0, 1, 7, 128, 8192, 3136):
+        for world in (1, 2, 3, 4, 8):
+            for r in range(world):
+                assert lc.shard_range(total, r, world) == shard_range(total, r, world)
+    with pytest.raises(ValueError):
+        lc.shard_range(10, 2, 2)
+
+
+def _failing_worker(rank, world, port, out_dir, bad_rank):
+    import datetime
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    status = "ok"
+    try:
+        if rank == bad_rank:
+            raise RuntimeError("injected failure before the gather")
+        local = torch.full((shard_range(6, rank, world)[1] - shard_range(6, rank, world)[0], 4), float(rank))
+        assemble(local, 6, rank, world)
+    except RuntimeError as exc:  # the failed peer surfaces as an error in the collective
+        status = f"error: {type(exc).__name__}"
+        if rank == bad_rank:
+            with open(os.path.join(out_dir, f"status_{rank}.txt"), "w") as f:
+                f.write(status)
+            raise
+    with open(os.path.join(out_dir, f"status_{rank}.txt"), "w") as f:
+        f.write(status)
+
+
+def test_rank_failure_surfaces_as_error_not_hang(tmp_path):
+    """A rank that fails before the assembling all-gather: every other rank's collective ends with
+    an error (closed connection or the 10 s process-group timeout), nobody hangs."""
+    import time
+
+    world, bad = 3, 1
+    t0 = time.time()
+    with pytest.raises(Exception):
+        mp.start_processes(_failing_worker, args=(world, _free_port(), str(tmp_path), bad), nprocs=world, join=True,
+                           start_method="spawn")
+    # the survivors finish on their own (join re-raised the bad rank's error first)
+    deadline = time.time() + 60
+    while time.time() < deadline and not all((tmp_path / f"status_{r}.txt").exists() for r in range(world)):
+        time.sleep(0.2)
+    assert time.time() - t0 < 90
+    for r in range(world):
+        status = (tmp_path / f"status_{r}.txt").read_text()
+        assert status.startswith("error"), (r, status)
