@@ -410,6 +410,18 @@ lcError_t lcConvAttentionNchwSharded(lcComm_t comm, const float* x, const float*
 lcError_t lcGetDeviceErrorWord(unsigned int* code);
 lcError_t lcClearDeviceErrorWord(void);
 
+/* ---- test hooks (no counterpart in the reference) -----------------------------------------
+ * For failure-path tests only; inert unless called.
+ * lcTestFailAllocations(after, count): of the library's next device allocations, `after` succeed
+ *   and the `count` after them fail (the op that needed them returns LC_OUT_OF_MEMORY, having
+ *   released what it already held); count = 0 disarms.
+ * lcTestStallNextGemm(kb): the next 1-SM tcgen05 GEMM launch ("tcgen05_128x256") leaves k-block kb
+ *   of its first tile unloaded, so the MMA warp's bounded mbarrier wait (2 s) runs out: the kernel
+ *   records the code in the device error word, drains its in-flight copies and MMAs, frees TMEM
+ *   and exits; a synchronising call returns LC_DRIVER_ERROR.  No fault, trap or hang is involved. */
+void lcTestFailAllocations(int after, int count);
+void lcTestStallNextGemm(int kblock);
+
 /* ---- runtime trace ring (src/runtime.cpp:63-99,620-760) ---------------------------------- */
 typedef struct lcRuntimeTraceEvent {
   int type;   /* RuntimeTraceEventType: 0 malloc .. 10 op_dispatch          */

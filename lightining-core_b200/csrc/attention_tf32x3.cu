@@ -574,29 +574,29 @@ bool attention_f32_tc_supported(const AttnArgs& a) {
          !(a.proj_w && a.post_relu) && tensor_map_encoder() != nullptr;
 }
 
+cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, size_t nv, int sp, DeviceCtx* ctx,
+                                    cudaStream_t s);
+
 cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
   const int sp = (a.seq + 3) & ~3;
   const size_t nqk = static_cast<size_t>(a.units) * a.seq * D, nv = static_cast<size_t>(a.units) * D * sp;
   const size_t bytes = (4 * nqk + 2 * nv) * sizeof(float);
-  // Split planes in a grow-only per-device workspace; `attn_tf32_done` orders the launches
-  // that use it one after another, whatever their streams.
-  std::lock_guard<std::mutex> lk(ctx->attn_tf32_mu);
-  cudaError_t e = cudaSuccess;
-  if (!ctx->attn_tf32_done) e = cudaEventCreateWithFlags(&ctx->attn_tf32_done, cudaEventDisableTiming);
+  // Split planes in a stream-ordered workspace: allocated and freed on `s` around the kernels, so
+  // calls on different streams run side by side.
+  float* ws = nullptr;
+  cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws), bytes, s);
   if (e != cudaSuccess) return e;
-  if (ctx->attn_tf32_bytes < bytes) {
-    if (ctx->attn_tf32_ws) {
-      if ((e = cudaEventSynchronize(ctx->attn_tf32_done)) != cudaSuccess) return e;
-      cudaFree(ctx->attn_tf32_ws);
-      ctx->attn_tf32_ws = nullptr;
-      ctx->attn_tf32_bytes = 0;
-    }
-    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->attn_tf32_ws), bytes)) != cudaSuccess) return e;
-    ctx->attn_tf32_bytes = bytes;
-  }
-  float* qh = ctx->attn_tf32_ws;
+  e = attention_f32_tc_planes(a, ws, nqk, nv, sp, ctx, s);
+  const cudaError_t ef = workspace_free(ws, s);
+  return e != cudaSuccess ? e : ef;
+}
+
+cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, size_t nv, int sp, DeviceCtx* ctx,
+                                    cudaStream_t s) {
+  cudaError_t e = cudaSuccess;
+  float* qh = ws;
   float* ql = qh + nqk;
   float* kh = ql + nqk;
   float* kl = kh + nqk;
@@ -614,7 +614,6 @@ cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
       return e;
     attr_set = true;
   }
-  if ((e = cudaStreamWaitEvent(s, ctx->attn_tf32_done, 0)) != cudaSuccess) return e;
   const dim3 sgrid(static_cast<unsigned>(std::min<long long>((static_cast<long long>(a.seq) * D / 4 + 255) / 256, 64)),
                    static_cast<unsigned>(a.units));
   split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.seq);
@@ -640,8 +639,7 @@ cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
   const long long grid = static_cast<long long>(p.nq) * a.units;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   fa_f32_tc_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  return cudaEventRecord(ctx->attn_tf32_done, s);
+  return cudaGetLastError();
 }
 
 }  // namespace lcb

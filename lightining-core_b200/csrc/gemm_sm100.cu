@@ -61,7 +61,7 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                        __nv_bfloat16* __restrict__ C, int M, int N, int K, unsigned* err_word) {
+                        __nv_bfloat16* __restrict__ C, int M, int N, int K, unsigned* err_word, int stall_kb) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
@@ -116,6 +116,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
             ok = false;
             break;
+          }
+          if (stall_kb == kb && t == 0) {
+            // Test hook (lcTestStallNextGemm): CTA 0 never fills this stage, so the MMA warp's
+            // bounded wait on it runs out and the CTA takes its abort path.
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
+            continue;
           }
           mbar_arrive_expect_tx(&st->full[stage], STAGE_BYTES);
           tma_load_2d(smem_a + stage * A_STAGE_BYTES, &map_a, kb * BK, mb * BM, &st->full[stage]);
@@ -558,7 +567,8 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bf
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-  gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, c, m, n, k, ctx->err_word);
+  gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ma, mb, c, m, n, k, ctx->err_word,
+                                                            take_gemm_stall_kblock());
   return cudaGetLastError();
 }
 

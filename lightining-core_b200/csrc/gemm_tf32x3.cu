@@ -469,26 +469,7 @@ struct Epi {
   int relu;
 };
 
-// Workspace of at least `bytes`, ordered after the previous 3xTF32 launch (caller holds tf32_mu).
-cudaError_t tf32_workspace(DeviceCtx* ctx, size_t bytes, cudaStream_t s) {
-  cudaError_t e = cudaSuccess;
-  if (!ctx->tf32_done && (e = cudaEventCreateWithFlags(&ctx->tf32_done, cudaEventDisableTiming)) != cudaSuccess)
-    return e;
-  if (ctx->tf32_ws_bytes < bytes) {
-    if (ctx->tf32_ws) {
-      if ((e = cudaEventSynchronize(ctx->tf32_done)) != cudaSuccess) return e;
-      cudaFree(ctx->tf32_ws);
-      ctx->tf32_ws = nullptr;
-      ctx->tf32_ws_bytes = 0;
-    }
-    if ((e = cudaMalloc(reinterpret_cast<void**>(&ctx->tf32_ws), bytes)) != cudaSuccess) return e;
-    ctx->tf32_ws_bytes = bytes;
-  }
-  return cudaStreamWaitEvent(s, ctx->tf32_done, 0);
-}
-
-// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each), then the event that
-// releases the workspace.
+// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each).
 cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
                           int m, int n, int kp, const Epi& epi, cudaStream_t s) {
   CUtensorMap mah, mal, mbh, mbl;
@@ -507,9 +488,7 @@ cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, 
   gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mah, mal, mbh, mbl, epi.c, m, n, kp, epi.period,
                                                            epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
                                                            ctx->err_word);
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) e = cudaEventRecord(ctx->tf32_done, s);
-  return e;
+  return cudaGetLastError();
 }
 
 int grid_for(long long n) { return static_cast<int>(n / 256 + 1 < 148 * 8 ? n / 256 + 1 : 148 * 8); }
@@ -520,17 +499,21 @@ cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
   const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
-  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
-  cudaError_t e = tf32_workspace(ctx, 2 * (na + nb) * sizeof(float), s);
+  // Split planes in a stream-ordered workspace: allocated and freed on `s` around the kernels.
+  float* ws = nullptr;
+  cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws), 2 * (na + nb) * sizeof(float), s);
   if (e != cudaSuccess) return e;
-  float* a_hi = ctx->tf32_ws;
+  float* a_hi = ws;
   float* a_lo = a_hi + na;
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
-  if ((e = split(a, a_hi, a_lo, na, s)) != cudaSuccess) return e;
-  tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  return launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s);
+  if ((e = split(a, a_hi, a_lo, na, s)) == cudaSuccess) {
+    tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
+    if ((e = cudaGetLastError()) == cudaSuccess)
+      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s);
+  }
+  const cudaError_t ef = workspace_free(ws, s);
+  return e != cudaSuccess ? e : ef;
 }
 
 // Conv as out_n[oc, p] = sum_kk W[oc, kk] col_n[kk, p] for all images at once: A = W [OC, C*kh*kw]
@@ -546,10 +529,10 @@ cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* 
   const long long rows = static_cast<long long>(batch) * oh * ow;
   if (rows > 0x7fffffffLL) return cudaErrorNotSupported;
   const size_t na = static_cast<size_t>(out_c) * kp, nb = static_cast<size_t>(rows) * kp;
-  std::lock_guard<std::mutex> lk(ctx->tf32_mu);
-  cudaError_t e = tf32_workspace(ctx, 2 * (na + nb) * sizeof(float), s);
+  float* ws = nullptr;
+  cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws), 2 * (na + nb) * sizeof(float), s);
   if (e != cudaSuccess) return e;
-  float* a_hi = ctx->tf32_ws;
+  float* a_hi = ws;
   float* a_lo = a_hi + na;
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
@@ -559,10 +542,13 @@ cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* 
     tf32_im2col_split_kernel<<<static_cast<unsigned>(blocks < 148 * 32 ? blocks : 148 * 32), 256, 0, s>>>(
         x, b_hi, b_lo, static_cast<int>(rows), k, kp, in_c, in_h, in_w, kh, kw, sh, sw, ph, pw, oh, ow);
   }
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  const int pix = oh * ow;
-  return launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, out_c, static_cast<int>(rows), kp,
-                       Epi{out, pix, static_cast<long long>(out_c) * pix, pix, bias, relu}, s);
+  if ((e = cudaGetLastError()) == cudaSuccess) {
+    const int pix = oh * ow;
+    e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, out_c, static_cast<int>(rows), kp,
+                      Epi{out, pix, static_cast<long long>(out_c) * pix, pix, bias, relu}, s);
+  }
+  const cudaError_t ef = workspace_free(ws, s);
+  return e != cudaSuccess ? e : ef;
 }
 
 // fp32 conv: the 3xTF32 tensor-core GEMM once the work covers its pre-pass (>= 2^28

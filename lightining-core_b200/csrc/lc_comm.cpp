@@ -274,7 +274,7 @@ lcError_t lcMatMulSharded(lcComm_t comm, const void* a, const void* b, void* out
       if (comm->b_stage) cudaFree(comm->b_stage);
       comm->b_stage = nullptr;
       comm->b_bytes = 0;
-      LC_TRY_CUDA(cudaMalloc(&comm->b_stage, bytes));
+      LC_TRY_CUDA(device_malloc(&comm->b_stage, bytes));
       comm->b_bytes = bytes;
     }
     size_t klo, khi;

@@ -16,18 +16,22 @@ struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
   unsigned* err_word = nullptr;  // device word written by kernels whose bounded waits gave up
-  // Split planes of the 3xTF32 GEMM (grow-only); `tf32_done` orders the launches that use them.
-  std::mutex tf32_mu;
-  float* tf32_ws = nullptr;
-  size_t tf32_ws_bytes = 0;
-  cudaEvent_t tf32_done = nullptr;
-  // Split planes of the 3xTF32 fp32 attention (grow-only), ordered the same way.
-  std::mutex attn_tf32_mu;
-  float* attn_tf32_ws = nullptr;
-  size_t attn_tf32_bytes = 0;
-  cudaEvent_t attn_tf32_done = nullptr;
+  // Stream-ordered pool for per-call workspaces (the 3xTF32 split planes): a call allocates on its
+  // own stream and frees on it after its kernels, so calls on different streams never wait for
+  // each other and no lock is held on the launch path.  Freed memory stays cached in the pool.
+  cudaMemPool_t pool = nullptr;
 };
 DeviceCtx* device_ctx();
+
+// Every device allocation of the library goes through these (so a test can make them fail).
+cudaError_t device_malloc(void** p, size_t bytes);
+// Stream-ordered workspace from the device pool; release with workspace_free on the same stream
+// after the kernels that use it.
+cudaError_t workspace_alloc(DeviceCtx* ctx, void** p, size_t bytes, cudaStream_t s);
+cudaError_t workspace_free(void* p, cudaStream_t s);
+// Test hook: when >= 0, the next 1-SM tcgen05 GEMM launch skips the loads of this k-block of its
+// first tile (its MMA warp's bounded wait then runs out); consumed by that launch.
+int take_gemm_stall_kblock();
 
 // ---- auto-tune cache (tune_cache.cpp); kind: LC_TUNE_MATMUL / LC_TUNE_ATTENTION -------------
 bool tune_lookup(int kind, size_t d0, size_t d1, size_t d2, int dtype, std::string* config);

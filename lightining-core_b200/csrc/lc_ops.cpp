@@ -36,7 +36,7 @@ struct Staging {
       s.ptr = nullptr;
       s.bytes = 0;
       const size_t want = bytes + bytes / 2;
-      cudaError_t e = cudaMalloc(&s.ptr, want);
+      cudaError_t e = device_malloc(&s.ptr, want);
       if (e != cudaSuccess) return e;
       s.bytes = want;
     }

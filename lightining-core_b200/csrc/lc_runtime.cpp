@@ -80,6 +80,45 @@ std::mutex g_ctx_mu;
 DeviceCtx* g_ctx[64] = {};
 }  // namespace
 
+std::mutex g_fail_mu;
+int g_fail_after = 0, g_fail_count = 0;  // test hook: let `after` allocations pass, fail `count`
+std::atomic<int> g_fail_armed{0};
+std::atomic<int> g_gemm_stall{-1};
+
+bool injected_alloc_failure() {
+  if (!g_fail_armed.load(std::memory_order_relaxed)) return false;
+  std::lock_guard<std::mutex> lk(g_fail_mu);
+  if (g_fail_after > 0) {
+    --g_fail_after;
+    return false;
+  }
+  if (g_fail_count > 0) {
+    if (--g_fail_count == 0) g_fail_armed.store(0);
+    return true;
+  }
+  return false;
+}
+
+cudaError_t device_malloc(void** p, size_t bytes) {
+  if (injected_alloc_failure()) {
+    *p = nullptr;
+    return cudaErrorMemoryAllocation;
+  }
+  return cudaMalloc(p, bytes);
+}
+
+cudaError_t workspace_alloc(DeviceCtx* ctx, void** p, size_t bytes, cudaStream_t s) {
+  if (injected_alloc_failure()) {
+    *p = nullptr;
+    return cudaErrorMemoryAllocation;
+  }
+  return cudaMallocFromPoolAsync(p, bytes, ctx->pool, s);
+}
+
+cudaError_t workspace_free(void* p, cudaStream_t s) { return p ? cudaFreeAsync(p, s) : cudaSuccess; }
+
+int take_gemm_stall_kblock() { return g_gemm_stall.exchange(-1); }
+
 DeviceCtx* device_ctx() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
@@ -89,12 +128,19 @@ DeviceCtx* device_ctx() {
   if (g_ctx[dev]) return g_ctx[dev];
   c = new DeviceCtx();
   c->device = dev;
+  cudaMemPoolProps props = {};
+  props.allocType = cudaMemAllocationTypePinned;
+  props.location.type = cudaMemLocationTypeDevice;
+  props.location.id = dev;
   if (cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
       cudaMalloc(&c->err_word, sizeof(unsigned)) != cudaSuccess ||
-      cudaMemset(c->err_word, 0, sizeof(unsigned)) != cudaSuccess) {
+      cudaMemset(c->err_word, 0, sizeof(unsigned)) != cudaSuccess || cudaMemPoolCreate(&c->pool, &props) != cudaSuccess) {
+    if (c->err_word) cudaFree(c->err_word);
     delete c;
     return nullptr;
   }
+  uint64_t keep = ~0ull;  // keep freed workspace cached in the pool instead of returning it
+  cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep);
   g_ctx[dev] = c;
   return c;
 }
@@ -111,7 +157,7 @@ lcError_t lcMalloc(void** ptr, size_t size_bytes) {
   if (ptr == nullptr || size_bytes == 0) {
     st = LC_INVALID_VALUE;
   } else {
-    st = from_cuda(cudaMalloc(ptr, size_bytes));
+    st = from_cuda(lcb::device_malloc(ptr, size_bytes));
   }
   trace_event(lcb::kTraceMalloc, st, size_bytes, 0, 0);
   return st;
@@ -351,5 +397,14 @@ lcError_t lcClearDeviceErrorWord(void) {
   if (!c) return LC_NOT_INITIALIZED;
   return from_cuda(cudaMemset(c->err_word, 0, sizeof(unsigned)));
 }
+
+void lcTestFailAllocations(int after, int count) {
+  std::lock_guard<std::mutex> lk(lcb::g_fail_mu);
+  lcb::g_fail_after = after < 0 ? 0 : after;
+  lcb::g_fail_count = count < 0 ? 0 : count;
+  lcb::g_fail_armed.store(lcb::g_fail_count > 0 ? 1 : 0);
+}
+
+void lcTestStallNextGemm(int kblock) { lcb::g_gemm_stall.store(kblock < 0 ? -1 : kblock); }
 
 }  // extern "C"

@@ -29,7 +29,7 @@ struct Buf {
 
 lcError_t alloc_all(Buf* bufs, int n) {
   for (int i = 0; i < n; ++i) {
-    if (cudaMalloc(&bufs[i].p, bufs[i].bytes) != cudaSuccess) {
+    if (lcb::device_malloc(&bufs[i].p, bufs[i].bytes) != cudaSuccess) {
       for (int j = 0; j < i; ++j) cudaFree(bufs[j].p);
       return LC_OUT_OF_MEMORY;
     }
@@ -160,7 +160,7 @@ lcError_t lcAttentionSessionTrainStep(lcAttentionSession_t s, const float* q, co
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (!s->target.p) {
     s->target.bytes = s->b[0].bytes;
-    if (cudaMalloc(&s->target.p, s->target.bytes) != cudaSuccess) {
+    if (lcb::device_malloc(&s->target.p, s->target.bytes) != cudaSuccess) {
       s->target.p = nullptr;
       return LC_OUT_OF_MEMORY;
     }

@@ -118,6 +118,8 @@ _SIGS = {
     "lcMatMulSessionRunBatch": (_i, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "lcAttentionTrainStep": (_i, [_vp] * 5 + [_f, _sz, _sz, _sz, _i, _vp, C.POINTER(AttentionIoPolicy), _vp]),
     "lcAttentionSessionTrainStep": (_i, [_vp] * 6 + [_f, _vp, C.POINTER(AttentionIoPolicy), _vp]),
+    "lcTestFailAllocations": (None, [_i, _i]),
+    "lcTestStallNextGemm": (None, [_i]),
     "lcCommAvailable": (_i, []),
     "lcCommGetUniqueId": (_i, [_vp]),
     "lcCommInitRank": (_i, [C.POINTER(_vp), _i, _vp, _i]),

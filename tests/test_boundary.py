@@ -149,3 +149,13 @@ def test_bf16_helpers(lc):
     x = np.random.default_rng(0).standard_normal(1000).astype(np.float32)
     from oracle import oracle as O
     np.testing.assert_array_equal(lc.from_bf16(lc.to_bf16(x)), O.port().bf16_round(x))
+
+
+def test_reference_c_example_links_against_this_library():
+    """The reference's own C example (examples/lightning_core_c_api.c), compiled unchanged against
+    include/lc_b200.h by `make -C oracle example`, resolves its lc* symbols from liblc_b200.so."""
+    exe = os.path.join(ROOT, "oracle", "_ref", "c_api_example")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/c_api_example not built (needs the reference sources)")
+    out = os.popen(f"ldd {exe}").read()
+    assert "liblc_b200.so" in out and "not found" not in out, out

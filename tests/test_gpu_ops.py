@@ -392,3 +392,20 @@ def test_matrix_sub_div(gpu):
     a = rng.uniform(-1, 1, 999)
     b = rng.uniform(0.5, 2, 999)
     np.testing.assert_array_equal(gpu.matrix_div(a, b, 9, 111), a / b)
+
+
+def test_reference_c_example_runs(gpu):
+    """The reference's unchanged C example, built against include/lc_b200.h and linked to
+    liblc_b200.so: lcMalloc / lcMemcpy both ways / lcDeviceSynchronize on the GPU, data round trip."""
+    import os
+    import subprocess
+
+    from conftest import ROOT
+
+    exe = os.path.join(ROOT, "oracle", "_ref", "c_api_example")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/c_api_example not built")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert "Lightning Core C API example: OK" in r.stdout
+    assert "backend=cuda" in r.stdout and "cuda=1" in r.stdout
