@@ -21,7 +21,7 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 P = O.port()
-ERR_GEMM_MMA_WAIT = 0x102
+ERR_GEMM_SITES = (0x101, 0x102, 0x103)  # producer / MMA / epilogue waits of the GEMM: whichever gives up first
 
 
 def _p(t):
@@ -51,7 +51,7 @@ def test_bounded_wait_timeout_reports_driver_error(gpu):
         assert 1.5 < took < 30, took  # the wait limit is 2 s
         code = C.c_uint()
         assert L.lcGetDeviceErrorWord(C.byref(code)) == gpu.LC_DRIVER_ERROR
-        assert code.value == ERR_GEMM_MMA_WAIT, hex(code.value)
+        assert code.value in ERR_GEMM_SITES, hex(code.value)
         # the context is still usable: clear, rerun, correct
         assert L.lcClearDeviceErrorWord() == gpu.LC_SUCCESS
         assert L.lcGetDeviceErrorWord(C.byref(code)) == gpu.LC_SUCCESS and code.value == 0
@@ -59,6 +59,7 @@ def test_bounded_wait_timeout_reports_driver_error(gpu):
         assert rc == gpu.LC_SUCCESS
     finally:
         L.lcTestStallNextGemm(-1)
+        L.lcClearDeviceErrorWord()  # never leave the word set for later tests
         gpu.tune_cache_reset()
     close_enough(P.matmul(a_h, b_h), c.float().cpu().numpy(), 2e-3, 2e-2)
 
