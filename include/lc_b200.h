@@ -189,6 +189,16 @@ void lcVectorAddIoPolicyDefault(lcVectorAddIoPolicy* p);
  * (start: upload, no download, no sync; run: nothing; finish: download+sync; sync: sync). */
 typedef enum lcLoopStage { LC_LOOP_START = 0, LC_LOOP_RUN, LC_LOOP_FINISH, LC_LOOP_SYNC } lcLoopStage;
 void lcMatMulPolicyForStage(lcLoopStage stage, lcMatMulIoPolicy* p);
+/* The same presets for vector add and the matrix elementwise ops (makeVectorPolicyForLoop /
+ * makeElemwisePolicyForLoop, include/lightning_core/core/model_customization.hpp:120-144, over the
+ * resident presets of ops/policy.hpp:73-150); both ops take lcVectorAddIoPolicy. */
+void lcVectorPolicyForStage(lcLoopStage stage, lcVectorAddIoPolicy* p);
+void lcElemwisePolicyForStage(lcLoopStage stage, lcVectorAddIoPolicy* p);
+/* makeAttentionPolicyForLoop (model_customization.hpp:146-185): sets only the transfer and sync
+ * flags of *p (loss_every and the output postprocess are the caller's): start uploads q, k, v and
+ * target; run moves nothing; finish downloads out (and v when `training`) and synchronizes; sync
+ * only synchronizes. */
+void lcAttentionPolicyForStage(lcLoopStage stage, int training, lcAttentionIoPolicy* p);
 
 /* Attention forward over `units` independent heads laid out [units, seq, head_dim].
  * Replaces attentionForwardWithPolicy (src/attention.cpp:137-201) for Device::kCUDA, batched.
@@ -337,7 +347,7 @@ lcError_t lcMatMulSessionRunBatch(lcMatMulSession_t s, const void* a, const void
  * means CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE, which is also loaded on first use and
  * rewritten whenever an entry is added.  Load rejects a file with an unknown header
  * (LC_NOT_SUPPORTED) and keeps the current rows. */
-typedef enum lcTuneKind { LC_TUNE_MATMUL = 0, LC_TUNE_ATTENTION = 1 } lcTuneKind;
+typedef enum lcTuneKind { LC_TUNE_MATMUL = 0, LC_TUNE_ATTENTION = 1, LC_TUNE_CONV = 2 } lcTuneKind;
 lcError_t lcTuneCacheLoad(lcTuneKind kind, const char* path);
 lcError_t lcTuneCacheSave(lcTuneKind kind, const char* path);
 /* Clears the cache (the reference's matMulMetalResetTuning, src/ops/matmul_metal.mm:1803-1834). */
@@ -403,6 +413,24 @@ lcError_t lcConvAttentionNchwSharded(lcComm_t comm, const float* x, const float*
                                      size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w, size_t seq,
                                      size_t head_dim, size_t proj_cols, const lcConv2dIoPolicy* policy,
                                      lcStream_t stream);
+
+/* Conv kernel-mode cache: the reference chooses the 3x3 conv kernel per shape and remembers it
+ * (chooseModeWithAutotune, src/ops/conv2d_metal.mm:577-672).  Here the LC_TUNE_CONV cache maps a
+ * conv shape to "simt" (implicit-GEMM CUDA-core kernel) or "tcgen05_3xtf32" (tensor-core 3xTF32
+ * GEMM over an im2col split); CJ_CONV_TUNE_CACHE_FILE persists it like the other kinds.  The shape
+ * is packed into the cache's three key columns by lcConvTuneKey (channels in d0, spatial size in
+ * d1, batch and kernel geometry in d2); shapes whose fields do not fit the packing
+ * (channels/extent >= 2^32, batch >= 2^32, kernel >= 256, stride/pad >= 16) return
+ * LC_NOT_SUPPORTED and are never cached. */
+lcError_t lcConvTuneKey(size_t batch, size_t in_channels, size_t in_h, size_t in_w, size_t out_channels,
+                        size_t kernel_h, size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h,
+                        size_t pad_w, size_t* d0, size_t* d1, size_t* d2);
+/* Times every conv kernel that can take the shape on the given device buffers (1 warm-up + median
+ * of 5), stores the fastest under the shape's key and writes its name to `best`.  Synchronizes. */
+lcError_t lcConvAutotune(const float* x, const float* w, const float* bias, float* out, size_t batch,
+                         size_t in_channels, size_t in_h, size_t in_w, size_t out_channels, size_t kernel_h,
+                         size_t kernel_w, size_t stride_h, size_t stride_w, size_t pad_h, size_t pad_w,
+                         int apply_relu, lcStream_t stream, char* best, size_t cap);
 
 /* ---- device error word: kernels' bounded waits record where they gave up ---------------- */
 /* Returns LC_DRIVER_ERROR and the recorded code if any kernel on the current device gave up a

@@ -598,6 +598,7 @@ cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloa
                       cudaStream_t s) {
   std::string cfg;
   const bool tuned = tune_lookup(LC_TUNE_MATMUL, m, k, n, 1 /*bf16*/, &cfg);
+  if ((tuned && cfg == kGemvName && m <= 2) || (!tuned && m <= 2)) return gemv_bf16(a, b, c, m, k, n, s);
   if ((tuned && cfg == "simt") || !gemm_bf16_tc_supported(a, b, c, m, k, n)) return gemm_bf16_simt(a, b, c, m, k, n, s);
   if (tuned && cfg == kGemmTc2Name) return gemm_bf16_tc2(a, b, c, m, k, n, s);
   if (tuned && cfg == kGemmTcName) return gemm_bf16_tc(a, b, c, m, k, n, s);

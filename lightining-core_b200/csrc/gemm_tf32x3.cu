@@ -18,6 +18,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <string>
+
 #include <mutex>
 
 #include "../../include/lc_b200.h"
@@ -551,16 +553,42 @@ cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* 
   return e != cudaSuccess ? e : ef;
 }
 
-// fp32 conv: the 3xTF32 tensor-core GEMM once the work covers its pre-pass (>= 2^28
-// multiply-adds), else the SIMT implicit GEMM.
+bool conv_tc_eligible(int in_c, int kh, int kw, int out_c) {
+  const long long kp = (static_cast<long long>(in_c) * kh * kw + 3) & ~3LL;
+  return out_c >= 32 && kp <= IM2COL_MAX_KP && kh < 256 && kw < 256 && in_c < 32768 && tensor_map_encoder() != nullptr;
+}
+
+bool conv_tune_key(size_t batch, size_t in_c, size_t in_h, size_t in_w, size_t out_c, size_t kh, size_t kw,
+                   size_t sh, size_t sw, size_t ph, size_t pw, size_t* d0, size_t* d1, size_t* d2) {
+  const size_t w32 = size_t(1) << 32;
+  if (batch >= w32 || in_c >= w32 || out_c >= w32 || in_h >= w32 || in_w >= w32 || kh >= 256 || kw >= 256 ||
+      sh >= 16 || sw >= 16 || ph >= 16 || pw >= 16)
+    return false;
+  *d0 = (in_c << 32) | out_c;
+  *d1 = (in_h << 32) | in_w;
+  *d2 = (batch << 32) | (kh << 24) | (kw << 16) | (sh << 12) | (sw << 8) | (ph << 4) | pw;
+  return true;
+}
+
+// fp32 conv: a cached per-shape choice (lcConvAutotune / lcTuneCacheSet under LC_TUNE_CONV) when
+// there is one; otherwise the 3xTF32 tensor-core GEMM once the work covers its pre-pass (>= 2^28
+// multiply-adds, >= 32 output channels), else the SIMT implicit GEMM.
 cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
                             int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
                             cudaStream_t s) {
+  const bool tc_ok = conv_tc_eligible(in_c, kh, kw, out_c);
+  size_t d0, d1, d2;
+  std::string cfg;
+  if (conv_tune_key(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, &d0, &d1, &d2) &&
+      tune_lookup(LC_TUNE_CONV, d0, d1, d2, LC_DTYPE_F32, &cfg)) {
+    if (cfg == kConvTcName && tc_ok)
+      return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
+    if (cfg == "simt")
+      return conv2d_nchw_f32_simt(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
+  }
   const long long oh = (in_h + 2 * ph - kh) / sh + 1, ow = (in_w + 2 * pw - kw) / sw + 1;
   const long long macs = static_cast<long long>(out_c) * batch * oh * ow * in_c * kh * kw;
-  const long long kp = (static_cast<long long>(in_c) * kh * kw + 3) & ~3LL;
-  if (macs >= (1LL << 28) && out_c >= 32 && kp <= IM2COL_MAX_KP && kh < 256 && kw < 256 && in_c < 32768 &&
-      tensor_map_encoder() != nullptr)
+  if (macs >= (1LL << 28) && out_c >= 32 && tc_ok)
     return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
   return conv2d_nchw_f32_simt(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
 }

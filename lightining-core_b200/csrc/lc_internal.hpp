@@ -57,6 +57,11 @@ cudaError_t gemm_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloa
 cudaError_t gemm_bf16_simt(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
                            cudaStream_t s);
 bool gemm_bf16_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n);
+// Small-M (m <= 2) matmul as a GEMV streaming B once (gemv.cu); tune-cache name "gemv".
+cudaError_t gemv_f32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s);
+cudaError_t gemv_bf16(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* c, int m, int k, int n,
+                      cudaStream_t s);
+constexpr const char* kGemvName = "gemv";
 // The two tcgen05 kernels by their tune-cache names: 1-SM 128x256 tiles, 2-SM (cluster pair) 256x256.
 constexpr const char* kGemmTcName = "tcgen05_128x256";
 constexpr const char* kGemmTc2Name = "tcgen05_2sm_256x256";
@@ -79,6 +84,12 @@ cudaError_t conv2d_nchw_f32_simt(const float* x, const float* w, const float* bi
 cudaError_t conv2d_nchw_f32_3xtf32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
                             int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw,
                             int relu, cudaStream_t s);
+// Tensor-core conv eligibility (shape limits of the im2col split) and the tune-cache key of a conv
+// shape (false: the shape does not fit the key packing and is never cached).
+bool conv_tc_eligible(int in_c, int kh, int kw, int out_c);
+bool conv_tune_key(size_t batch, size_t in_c, size_t in_h, size_t in_w, size_t out_c, size_t kh, size_t kw,
+                   size_t sh, size_t sw, size_t ph, size_t pw, size_t* d0, size_t* d1, size_t* d2);
+constexpr const char* kConvTcName = "tcgen05_3xtf32";
 // Cyclic repeat of the first `have` floats of src into dst[0, total) (qkv_pack short case).
 cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s);
 

@@ -238,6 +238,24 @@ void lcMatMulPolicyForStage(lcLoopStage stage, lcMatMulIoPolicy* p) {
   p->synchronize = stage == LC_LOOP_FINISH || stage == LC_LOOP_SYNC;
 }
 
+void lcVectorPolicyForStage(lcLoopStage stage, lcVectorAddIoPolicy* p) {
+  if (!p) return;
+  p->upload_a = p->upload_b = stage == LC_LOOP_START;
+  p->download_out = stage == LC_LOOP_FINISH;
+  p->synchronize = stage == LC_LOOP_FINISH || stage == LC_LOOP_SYNC;
+}
+
+void lcElemwisePolicyForStage(lcLoopStage stage, lcVectorAddIoPolicy* p) { lcVectorPolicyForStage(stage, p); }
+
+void lcAttentionPolicyForStage(lcLoopStage stage, int training, lcAttentionIoPolicy* p) {
+  if (!p) return;
+  const int start = stage == LC_LOOP_START, finish = stage == LC_LOOP_FINISH;
+  p->upload_q = p->upload_k = p->upload_v = p->upload_target = start;
+  p->download_out = finish;
+  p->download_v = finish && training;
+  p->synchronize = finish || stage == LC_LOOP_SYNC;
+}
+
 lcError_t lcAttentionForward(const void* q, const void* k, const void* v, void* out, size_t units, size_t seq,
                              size_t head_dim, int causal, lcDataType dtype, const lcAttentionIoPolicy* policy,
                              lcStream_t stream) {

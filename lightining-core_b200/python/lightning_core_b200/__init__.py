@@ -31,7 +31,7 @@ LC_SUCCESS, LC_NOT_INITIALIZED, LC_INVALID_VALUE, LC_OUT_OF_MEMORY, LC_NOT_SUPPO
 H2H, H2D, D2H, D2D = range(4)
 F32, BF16, F64 = 0, 1, 2
 LOOP_START, LOOP_RUN, LOOP_FINISH, LOOP_SYNC = range(4)
-TUNE_MATMUL, TUNE_ATTENTION = 0, 1
+TUNE_MATMUL, TUNE_ATTENTION, TUNE_CONV = 0, 1, 2
 
 
 class AttentionIoPolicy(C.Structure):
@@ -79,6 +79,9 @@ _SIGS = {
     "lcConv2dIoPolicyDefault": (None, [C.POINTER(Conv2dIoPolicy)]),
     "lcVectorAddIoPolicyDefault": (None, [C.POINTER(VectorAddIoPolicy)]),
     "lcMatMulPolicyForStage": (None, [_i, C.POINTER(MatMulIoPolicy)]),
+    "lcVectorPolicyForStage": (None, [_i, C.POINTER(VectorAddIoPolicy)]),
+    "lcElemwisePolicyForStage": (None, [_i, C.POINTER(VectorAddIoPolicy)]),
+    "lcAttentionPolicyForStage": (None, [_i, _i, C.POINTER(AttentionIoPolicy)]),
     "lcAttentionForward": (_i, [_vp, _vp, _vp, _vp, _sz, _sz, _sz, _i, _i, C.POINTER(AttentionIoPolicy), _vp]),
     "lcMatMul": (_i, [_vp, _vp, _vp, _sz, _sz, _sz, _i, C.POINTER(MatMulIoPolicy), _vp]),
     "lcConv2dNchw": (_i, [_vp, _vp, _vp, _vp] + [_sz] * 11 + [_i, C.POINTER(Conv2dIoPolicy), _vp]),
@@ -120,6 +123,8 @@ _SIGS = {
     "lcAttentionSessionTrainStep": (_i, [_vp] * 6 + [_f, _vp, C.POINTER(AttentionIoPolicy), _vp]),
     "lcTestFailAllocations": (None, [_i, _i]),
     "lcTestStallNextGemm": (None, [_i]),
+    "lcConvTuneKey": (_i, [_sz] * 11 + [C.POINTER(_sz)] * 3),
+    "lcConvAutotune": (_i, [_vp] * 4 + [_sz] * 11 + [_i, _vp, C.c_char_p, _sz]),
     "lcCommAvailable": (_i, []),
     "lcCommGetUniqueId": (_i, [_vp]),
     "lcCommInitRank": (_i, [C.POINTER(_vp), _i, _vp, _i]),
@@ -676,3 +681,11 @@ def shard_range(total: int, rank: int, nranks: int) -> tuple[int, int]:
     if lib.lcShardRange(total, rank, nranks, C.byref(lo), C.byref(hi)) != LC_SUCCESS:
         raise ValueError("bad shard request")
     return lo.value, hi.value
+
+
+def conv_tune_key(batch, in_c, in_h, in_w, out_c, kh, kw, sh=1, sw=1, ph=0, pw=0):
+    """The LC_TUNE_CONV cache key (d0, d1, d2) of a conv shape (lcConvTuneKey)."""
+    d = [C.c_size_t() for _ in range(3)]
+    check(lib.lcConvTuneKey(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, *(C.byref(x) for x in d)),
+          "conv_tune_key")
+    return tuple(x.value for x in d)

@@ -117,6 +117,32 @@ def test_policy_defaults_and_loop_presets(lc):
     for stage, want in table.items():
         q = lc.matmul_policy_for_stage(stage)
         assert (q.upload_a, q.upload_b, q.download_out, q.synchronize) == want
+        for fn in (lc.lib.lcVectorPolicyForStage, lc.lib.lcElemwisePolicyForStage):
+            v = lc.VectorAddIoPolicy()
+            fn(stage, C.byref(v))
+            assert (v.upload_a, v.upload_b, v.download_out, v.synchronize) == want
+
+
+def test_attention_loop_presets(lc):
+    """makeAttentionPolicyForLoop (include/lightning_core/core/model_customization.hpp:146-185): the
+    transfer/sync flags per stage; loss_every and the postprocess are left as the caller set them."""
+    flags = ("upload_q", "upload_k", "upload_v", "upload_target", "download_out", "download_v", "synchronize")
+    table = {lc.LOOP_START: (1, 1, 1, 1, 0, 0, 0), lc.LOOP_RUN: (0,) * 7, lc.LOOP_SYNC: (0,) * 6 + (1,)}
+    for training in (0, 1):
+        table[lc.LOOP_FINISH] = (0, 0, 0, 0, 1, training, 1)
+        for stage, want in table.items():
+            p = lc.default_attention_policy()
+            p.loss_every, p.output_scale, p.output_bias, p.output_relu = 8, 0.5, -1.0, 1
+            lc.lib.lcAttentionPolicyForStage(stage, training, C.byref(p))
+            assert tuple(getattr(p, f) for f in flags) == want, (stage, training)
+            assert (p.loss_every, p.output_scale, p.output_bias, p.output_relu) == (8, 0.5, -1.0, 1)
+
+
+def test_conv_tune_key_packing(lc):
+    d = lc.conv_tune_key(32, 64, 56, 56, 192, 3, 3, 1, 1, 1, 1)
+    assert d == ((64 << 32) | 192, (56 << 32) | 56, (32 << 32) | (3 << 24) | (3 << 16) | (1 << 12) | (1 << 8) | (1 << 4) | 1)
+    with pytest.raises(lc.LightningError):
+        lc.conv_tune_key(1, 3, 8, 8, 4, 3, 3, 16, 1, 0, 0)  # stride does not fit the key
 
 
 def test_trace_ring(lc):

@@ -9,11 +9,11 @@ from conftest import close_enough
 
 @pytest.fixture(autouse=True)
 def _clean(lc):
-    lc.lib.lcTuneCacheReset(lc.TUNE_MATMUL)
-    lc.lib.lcTuneCacheReset(lc.TUNE_ATTENTION)
+    for kind in (lc.TUNE_MATMUL, lc.TUNE_ATTENTION, lc.TUNE_CONV):
+        lc.lib.lcTuneCacheReset(kind)
     yield
-    lc.lib.lcTuneCacheReset(lc.TUNE_MATMUL)
-    lc.lib.lcTuneCacheReset(lc.TUNE_ATTENTION)
+    for kind in (lc.TUNE_MATMUL, lc.TUNE_ATTENTION, lc.TUNE_CONV):
+        lc.lib.lcTuneCacheReset(kind)
 
 
 def test_roundtrip_v2(lc, tmp_path):
@@ -128,3 +128,80 @@ def test_attention_autotune_records_and_is_used(gpu, dtype, d, causal):
     tol = (1e-4, 1e-4) if dt == gpu.F32 else (2e-2, 2e-2)
     for u in range(units):
         close_enough(O.port().attention(q[u], k[u], v[u], bool(causal)), got[u], *tol)
+
+
+def test_conv_cache_roundtrip(lc, tmp_path):
+    """The conv kind uses the same file format: `#lc_tune_cache,conv,2` with packed shape keys."""
+    key = lc.conv_tune_key(32, 64, 56, 56, 192, 3, 3, 1, 1, 1, 1)
+    lc.tune_cache_set(lc.TUNE_CONV, *key, "tcgen05_3xtf32", lc.F32)
+    path = str(tmp_path / "conv.csv")
+    assert lc.lib.lcTuneCacheSave(lc.TUNE_CONV, path.encode()) == lc.LC_SUCCESS
+    lines = open(path).read().splitlines()
+    assert lines[0] == "#lc_tune_cache,conv,2" and lines[1].startswith("#columns,")
+    lc.lib.lcTuneCacheReset(lc.TUNE_CONV)
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_CONV, path.encode()) == lc.LC_SUCCESS
+    assert lc.tune_cache_get(lc.TUNE_CONV, *key, lc.F32) == "tcgen05_3xtf32"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (2, 4096, 777), (1, 3, 5), (2, 8192, 8), (1, 50000, 96)])
+def test_small_m_gemv(gpu, dtype, m, k, n):
+    """m <= 2 runs the GEMV (the reference's small-M path, src/ops/matmul_metal.mm:795-863), by
+    default and pinned; against the oracle; the autotune offers it and its result is used."""
+    from oracle import oracle as O
+
+    P = O.port()
+    rng = np.random.default_rng(m * 7 + n)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = (rng.uniform(-1, 1, (k, n)) / np.sqrt(k)).astype(np.float32)
+    dt = gpu.F32 if dtype == "f32" else gpu.BF16
+    if dt == gpu.BF16:
+        a, b = P.bf16_round(a), P.bf16_round(b)
+    ref = P.matmul(a, b)
+    tol = (1e-4, 1e-4) if dt == gpu.F32 else (2e-3, 2e-2)
+    conv = (lambda x: x) if dt == gpu.F32 else gpu.from_bf16
+    ha, hb = (a, b) if dt == gpu.F32 else (gpu.to_bf16(a), gpu.to_bf16(b))
+    close_enough(ref, conv(gpu.matmul2d(ha, hb, dtype=dt)), *tol)
+    gpu.tune_cache_set(gpu.TUNE_MATMUL, m, k, n, "gemv", dt)
+    close_enough(ref, conv(gpu.matmul2d(ha, hb, dtype=dt)), *tol)
+    gpu.lib.lcTuneCacheReset(gpu.TUNE_MATMUL)
+    da, db = gpu.DeviceBuffer.from_array(ha), gpu.DeviceBuffer.from_array(hb)
+    dc = gpu.DeviceBuffer(m * n * (4 if dt == gpu.F32 else 2))
+    best = gpu.matmul_autotune(da, db, dc, m, k, n, dt)
+    assert gpu.tune_cache_get(gpu.TUNE_MATMUL, m, k, n, dt) == best
+    close_enough(ref, conv(gpu.matmul2d(ha, hb, dtype=dt)), *tol)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(2, 64, 56, 56, 192, 1, 1), (3, 8, 12, 12, 24, 1, 1), (1, 32, 30, 30, 64, 2, 0)])
+def test_conv_modes_and_autotune(gpu, shape):
+    """The conv kernel-mode cache (the reference's chooseModeWithAutotune,
+    src/ops/conv2d_metal.mm:577-672): every mode pinned through LC_TUNE_CONV matches the oracle, and
+    lcConvAutotune stores a mode that is then used."""
+    import ctypes as C
+
+    from oracle import oracle as O
+
+    P = O.port()
+    n, c, h, w_, oc, st, pd = shape
+    rng = np.random.default_rng(n + c + oc)
+    x = rng.standard_normal((n, c, h, w_)).astype(np.float32)
+    w = rng.uniform(-0.2, 0.2, (oc, c, 3, 3)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, oc).astype(np.float32)
+    ref = P.conv2d(x, w, bias, (st, st), (pd, pd), True)
+    key = gpu.conv_tune_key(n, c, h, w_, oc, 3, 3, st, st, pd, pd)
+    modes = ["simt"] + (["tcgen05_3xtf32"] if oc >= 32 else [])
+    for mode in modes:
+        gpu.tune_cache_set(gpu.TUNE_CONV, *key, mode, gpu.F32)
+        close_enough(ref, gpu.conv2d_nchw(x, w, bias, st, st, pd, pd, apply_relu=True), 1e-4, 1e-4)
+    gpu.lib.lcTuneCacheReset(gpu.TUNE_CONV)
+    dx, dw, db = (gpu.DeviceBuffer.from_array(t) for t in (x, w, bias))
+    dout = gpu.DeviceBuffer(ref.size * 4)
+    best = C.create_string_buffer(64)
+    gpu.check(gpu.lib.lcConvAutotune(dx.ptr, dw.ptr, db.ptr, dout.ptr, n, c, h, w_, oc, 3, 3, st, st, pd, pd, 1,
+                                     None, best, 64), "lcConvAutotune")
+    assert best.value.decode() in modes
+    assert gpu.tune_cache_get(gpu.TUNE_CONV, *key, gpu.F32) == best.value.decode()
+    close_enough(ref, dout.download(ref.shape, np.float32), 1e-4, 1e-4)
+    close_enough(ref, gpu.conv2d_nchw(x, w, bias, st, st, pd, pd, apply_relu=True), 1e-4, 1e-4)
