@@ -416,8 +416,10 @@ lcError_t lcConvAttentionNchwSharded(lcComm_t comm, const float* x, const float*
 
 /* Conv kernel-mode cache: the reference chooses the 3x3 conv kernel per shape and remembers it
  * (chooseModeWithAutotune, src/ops/conv2d_metal.mm:577-672).  Here the LC_TUNE_CONV cache maps a
- * conv shape to "simt" (implicit-GEMM CUDA-core kernel) or "tcgen05_3xtf32" (tensor-core 3xTF32
- * GEMM over an im2col split); CJ_CONV_TUNE_CACHE_FILE persists it like the other kinds.  The shape
+ * conv shape to "simt" (implicit-GEMM CUDA-core kernel), "tcgen05_implicit" (implicit-GEMM 3xTF32
+ * tensor-core kernel: in_channels % 32 == 0, 16 <= out_channels <= 256, out_channels % 16 == 0) or
+ * "tcgen05_3xtf32" (tensor-core 3xTF32 GEMM over an im2col split held in a workspace);
+ * CJ_CONV_TUNE_CACHE_FILE persists it like the other kinds.  The shape
  * is packed into the cache's three key columns by lcConvTuneKey (channels in d0, spatial size in
  * d1, batch and kernel geometry in d2); shapes whose fields do not fit the packing
  * (channels/extent >= 2^32, batch >= 2^32, kernel >= 256, stride/pad >= 16) return

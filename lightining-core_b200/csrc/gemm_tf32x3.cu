@@ -571,8 +571,9 @@ bool conv_tune_key(size_t batch, size_t in_c, size_t in_h, size_t in_w, size_t o
 }
 
 // fp32 conv: a cached per-shape choice (lcConvAutotune / lcTuneCacheSet under LC_TUNE_CONV) when
-// there is one; otherwise the 3xTF32 tensor-core GEMM once the work covers its pre-pass (>= 2^28
-// multiply-adds, >= 32 output channels), else the SIMT implicit GEMM.
+// there is one; otherwise the implicit-GEMM tensor-core kernel for shapes it takes (>= 2^26
+// multiply-adds), the im2col 3xTF32 GEMM for other large shapes (>= 2^28 multiply-adds, >= 32
+// output channels), else the SIMT implicit GEMM.
 cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
                             int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
                             cudaStream_t s) {
@@ -581,6 +582,8 @@ cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, f
   std::string cfg;
   if (conv_tune_key(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, &d0, &d1, &d2) &&
       tune_lookup(LC_TUNE_CONV, d0, d1, d2, LC_DTYPE_F32, &cfg)) {
+    if (cfg == kConvImplicitName && conv_implicit_supported(in_c, out_c, kh, kw))
+      return conv2d_nchw_f32_implicit(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
     if (cfg == kConvTcName && tc_ok)
       return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
     if (cfg == "simt")
@@ -588,6 +591,8 @@ cudaError_t conv2d_nchw_f32(const float* x, const float* w, const float* bias, f
   }
   const long long oh = (in_h + 2 * ph - kh) / sh + 1, ow = (in_w + 2 * pw - kw) / sw + 1;
   const long long macs = static_cast<long long>(out_c) * batch * oh * ow * in_c * kh * kw;
+  if (macs >= (1LL << 26) && conv_implicit_supported(in_c, out_c, kh, kw))
+    return conv2d_nchw_f32_implicit(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
   if (macs >= (1LL << 28) && out_c >= 32 && tc_ok)
     return conv2d_nchw_f32_3xtf32(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);
   return conv2d_nchw_f32_simt(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, s);

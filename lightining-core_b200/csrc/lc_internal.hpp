@@ -90,6 +90,13 @@ bool conv_tc_eligible(int in_c, int kh, int kw, int out_c);
 bool conv_tune_key(size_t batch, size_t in_c, size_t in_h, size_t in_w, size_t out_c, size_t kh, size_t kw,
                    size_t sh, size_t sw, size_t ph, size_t pw, size_t* d0, size_t* d1, size_t* d2);
 constexpr const char* kConvTcName = "tcgen05_3xtf32";
+// Implicit-GEMM 3xTF32 conv (conv_implicit_sm100.cu): im2col gathered into shared memory by the
+// kernel itself; in_channels % 32 == 0, 16 <= out_channels <= 256, out_channels % 16 == 0.
+bool conv_implicit_supported(int in_c, int out_c, int kh, int kw);
+cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float* bias, float* out, int batch,
+                                     int in_c, int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph,
+                                     int pw, int relu, cudaStream_t s);
+constexpr const char* kConvImplicitName = "tcgen05_implicit";
 // Cyclic repeat of the first `have` floats of src into dst[0, total) (qkv_pack short case).
 cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s);
 

@@ -415,7 +415,10 @@ lcError_t lcConvAutotune(const float* x, const float* w, const float* bias, floa
             PW = (int)pad_w, R = apply_relu ? 1 : 0;
   std::vector<std::string> cands = {"simt"};
   if (conv_tc_eligible(C, KH, KW, OC)) cands.push_back(kConvTcName);
+  if (conv_implicit_supported(C, OC, KH, KW)) cands.push_back(kConvImplicitName);
   auto run = [&](const std::string& c) -> cudaError_t {
+    if (c == kConvImplicitName)
+      return conv2d_nchw_f32_implicit(x, w, bias, out, B, C, H, W, OC, KH, KW, SH, SW, PH, PW, R, s);
     return c == kConvTcName ? conv2d_nchw_f32_3xtf32(x, w, bias, out, B, C, H, W, OC, KH, KW, SH, SW, PH, PW, R, s)
                             : conv2d_nchw_f32_simt(x, w, bias, out, B, C, H, W, OC, KH, KW, SH, SW, PH, PW, R, s);
   };

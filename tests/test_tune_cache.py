@@ -174,7 +174,9 @@ def test_small_m_gemv(gpu, dtype, m, k, n):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shape", [(2, 64, 56, 56, 192, 1, 1), (3, 8, 12, 12, 24, 1, 1), (1, 32, 30, 30, 64, 2, 0)])
+@pytest.mark.parametrize("shape", [(2, 64, 56, 56, 192, 1, 1, 3), (3, 8, 12, 12, 24, 1, 1, 3),
+                                   (1, 32, 30, 30, 64, 2, 0, 3), (2, 32, 17, 23, 48, 1, 2, 5),
+                                   (3, 96, 9, 9, 256, 1, 1, 3), (1, 64, 7, 7, 16, 1, 0, 1)])
 def test_conv_modes_and_autotune(gpu, shape):
     """The conv kernel-mode cache (the reference's chooseModeWithAutotune,
     src/ops/conv2d_metal.mm:577-672): every mode pinned through LC_TUNE_CONV matches the oracle, and
@@ -184,14 +186,15 @@ def test_conv_modes_and_autotune(gpu, shape):
     from oracle import oracle as O
 
     P = O.port()
-    n, c, h, w_, oc, st, pd = shape
+    n, c, h, w_, oc, st, pd, ks = shape
     rng = np.random.default_rng(n + c + oc)
     x = rng.standard_normal((n, c, h, w_)).astype(np.float32)
-    w = rng.uniform(-0.2, 0.2, (oc, c, 3, 3)).astype(np.float32)
+    w = rng.uniform(-0.2, 0.2, (oc, c, ks, ks)).astype(np.float32)
     bias = rng.uniform(-0.1, 0.1, oc).astype(np.float32)
     ref = P.conv2d(x, w, bias, (st, st), (pd, pd), True)
-    key = gpu.conv_tune_key(n, c, h, w_, oc, 3, 3, st, st, pd, pd)
+    key = gpu.conv_tune_key(n, c, h, w_, oc, ks, ks, st, st, pd, pd)
     modes = ["simt"] + (["tcgen05_3xtf32"] if oc >= 32 else [])
+    modes += ["tcgen05_implicit"] if c % 32 == 0 and oc % 16 == 0 and 16 <= oc <= 256 else []
     for mode in modes:
         gpu.tune_cache_set(gpu.TUNE_CONV, *key, mode, gpu.F32)
         close_enough(ref, gpu.conv2d_nchw(x, w, bias, st, st, pd, pd, apply_relu=True), 1e-4, 1e-4)
@@ -199,7 +202,7 @@ def test_conv_modes_and_autotune(gpu, shape):
     dx, dw, db = (gpu.DeviceBuffer.from_array(t) for t in (x, w, bias))
     dout = gpu.DeviceBuffer(ref.size * 4)
     best = C.create_string_buffer(64)
-    gpu.check(gpu.lib.lcConvAutotune(dx.ptr, dw.ptr, db.ptr, dout.ptr, n, c, h, w_, oc, 3, 3, st, st, pd, pd, 1,
+    gpu.check(gpu.lib.lcConvAutotune(dx.ptr, dw.ptr, db.ptr, dout.ptr, n, c, h, w_, oc, ks, ks, st, st, pd, pd, 1,
                                      None, best, 64), "lcConvAutotune")
     assert best.value.decode() in modes
     assert gpu.tune_cache_get(gpu.TUNE_CONV, *key, gpu.F32) == best.value.decode()
