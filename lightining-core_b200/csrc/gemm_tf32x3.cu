@@ -32,16 +32,13 @@ void* tensor_map_encoder();
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 32, STAGES = 3;
+constexpr int BM = 128, BK = 32, STAGES = 3;
 constexpr int CHUNK_KB = 4;   // k-blocks (of 32) per TMEM partial sum: 128-deep K chunks
-constexpr int ACC_BUFS = 4;   // TMEM partial-sum buffers of BN columns
+constexpr int ACC_BUFS = 4;   // TMEM partial-sum buffers of BN (<= 128) columns
 constexpr int NUM_THREADS = 192;
 constexpr int A_PLANE_BYTES = BM * BK * 4;        // 16 KB
-constexpr int B_PLANE_BYTES = BN * BK * 4;        // 16 KB: 128 B^T rows x 32 K
-constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * B_PLANE_BYTES;  // hi + lo of each
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
-constexpr uint32_t IDESC = idesc_tf32_f32(BM, BN, /*a_mn_major=*/0, /*b_mn_major=*/0);
 
 struct Tail {
   uint64_t full[STAGES];
@@ -52,7 +49,6 @@ struct Tail {
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + sizeof(Tail);
 
 // x rounded to the 10-bit tf32 mantissa (nearest, ties away from zero), kept in fp32 layout with the
 // 13 low mantissa bits clear: add half a tf32 unit (bit 12) to the magnitude, then truncate.
@@ -195,11 +191,17 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   nb = r / gm;
 }
 
+// BN_T: output columns per tile (128, or 64 when 128-wide tiles would leave SMs idle).
+template <int BN_T>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                        const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                        float* __restrict__ C, int M, int N, int K, int period, long long batch_stride,
                        long long row_stride, const float* __restrict__ row_bias, int relu, unsigned* err_word) {
+  constexpr int BN = BN_T;
+  constexpr int B_PLANE_BYTES = BN * BK * 4;
+  constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * B_PLANE_BYTES;
+  constexpr uint32_t IDESC = idesc_tf32_f32(BM, BN, /*a_mn_major=*/0, /*b_mn_major=*/0);
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // Stage layout: A_hi | A_lo | B_hi | B_lo.
@@ -471,25 +473,36 @@ struct Epi {
   int relu;
 };
 
-// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each).
+size_t smem_bytes_for(int bn) { return 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * bn * BK * 4) + sizeof(Tail); }
+
+// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each), with bn-column tiles
+// (128, or 64 when 128-wide tiles would leave SMs idle: 1024^3 has 64 tiles of 128x128 for 148 SMs).
 cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                          int m, int n, int kp, const Epi& epi, cudaStream_t s) {
+                          int m, int n, int kp, const Epi& epi, cudaStream_t s, int bn = 128) {
   CUtensorMap mah, mal, mbh, mbl;
   if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
-      !make_tmap_f32_2d(&mbh, b_hi, n, kp, BN, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, BN, BK))
+      !make_tmap_f32_2d(&mbh, b_hi, n, kp, bn, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, bn, BK))
     return cudaErrorInvalidValue;
   static bool attr_set = false;  // benign race: idempotent attribute set
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SMEM_BYTES));
+    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes_for(128)));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemm_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem_bytes_for(64)));
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
+  const int tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
-  gemm_tf32x3_kernel<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(mah, mal, mbh, mbl, epi.c, m, n, kp, epi.period,
-                                                           epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
-                                                           ctx->err_word);
+  if (bn == 64)
+    gemm_tf32x3_kernel<64><<<grid, NUM_THREADS, smem_bytes_for(64), s>>>(
+        mah, mal, mbh, mbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+        ctx->err_word);
+  else
+    gemm_tf32x3_kernel<128><<<grid, NUM_THREADS, smem_bytes_for(128), s>>>(
+        mah, mal, mbh, mbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+        ctx->err_word);
   return cudaGetLastError();
 }
 
@@ -512,7 +525,8 @@ cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int
   if ((e = split(a, a_hi, a_lo, na, s)) == cudaSuccess) {
     tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
     if ((e = cudaGetLastError()) == cudaSuccess)
-      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s);
+      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s,
+                        static_cast<long long>((m + BM - 1) / BM) * ((n + 127) / 128) < ctx->sm_count ? 64 : 128);
   }
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
