@@ -58,7 +58,22 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const T* __restrict__ a,
   const int k0 = blockIdx.y * kchunk;
   const int k1 = min(k, k0 + kchunk);
   float acc[MR][4] = {};
-  for (int kk = k0 + kl; kk < k1; kk += kLanesK) {
+  int kk = k0 + kl;
+  // Four B rows per iteration: their loads are independent, so four are in flight per thread.
+  for (; kk + 3 * kLanesK < k1; kk += 4 * kLanesK) {
+    float bv[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) load4(b + static_cast<long long>(kk + u * kLanesK) * n, col0, n, vec, bv[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int r = 0; r < MR; ++r) {
+        const float av = to_f(a[static_cast<long long>(r) * k + kk + u * kLanesK]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[r][j] = fmaf(av, bv[u][j], acc[r][j]);
+      }
+  }
+  for (; kk < k1; kk += kLanesK) {
     float bv[4];
     load4(b + static_cast<long long>(kk) * n, col0, n, vec, bv);
 #pragma unroll
