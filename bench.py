@@ -637,7 +637,8 @@ def main():
         import torch.distributed as dist
 
         # NCCL's init lines (transport per channel: P2P/NVLS/...) go to stderr for the record.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT,GRAPH,NVLS")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
