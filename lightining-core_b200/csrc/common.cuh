@@ -135,6 +135,18 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Im2col-mode 4-D TMA load (tensor [n, h, w, c] fp32, coordinates {c, w, h, n} of the pixel box's
+// first pixel, plus the kernel-tap offsets {w, h}); completion counted on `bar`.  No multicast.
+__device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const CUtensorMap* map, int c, int w, int h, int n,
+                                                   uint16_t off_w, uint16_t off_h, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(smem_u32(bar)), "h"(off_w),
+      "h"(off_h)
+      : "memory");
+}
+
 // 3-D TMA store shared -> global (bulk async-group completion).  Rows outside the tensor map's
 // extent are not written.  The smem writes it reads must precede a fence.proxy.async.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {

@@ -23,6 +23,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 #include "../../include/lc_b200.h"
 #include "common.cuh"
 #include "lc_internal.hpp"
@@ -74,8 +76,12 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(u);
 }
 
+// TMA_A: the im2col tiles come from TMA im2col-mode loads of pre-split NHWC planes (map_xhi /
+// map_xlo) issued by one thread, instead of being gathered and split by the producer warps.
+template <bool TMA_A>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     conv_implicit_tf32x3_kernel(const __grid_constant__ CUtensorMap map_whi, const __grid_constant__ CUtensorMap map_wlo,
+                                const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                                 const ConvParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -103,6 +109,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_barrier_init();
     tma_prefetch_desc(&map_whi);
     tma_prefetch_desc(&map_wlo);
+    if (TMA_A) {
+      tma_prefetch_desc(&map_xhi);
+      tma_prefetch_desc(&map_xlo);
+    }
   }
   if (warp == 0) {
     tmem_alloc(&st->tmem_base, TMEM_COLS);
@@ -114,7 +124,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
 
-  if (warp < NUM_PRODUCER_WARPS) {
+  if (TMA_A && warp < NUM_PRODUCER_WARPS) {
+    // ---------------- one thread: TMA im2col loads of the A planes + the weight planes --------
+    if (warp == 0 && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        // The tile's first output pixel: (n, oy, ox) -> input coordinates of its top-left tap.
+        const int gp = t * BM;
+        const int n = gp / pix_img, pp = gp - n * pix_img;
+        const int oy = pp / p.ow, ox = pp - oy * p.ow;
+        const int w0 = ox * p.sw - p.pw, h0 = oy * p.sh - p.ph;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, p.err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          uint8_t* base = smem + stage * stage_bytes;
+          const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * BK;
+          const int dy = tap / p.kw, dx = tap - dy * p.kw;
+          mbar_arrive_expect_tx(&st->b_full[stage], 2 * A_PLANE_BYTES + 2 * b_plane);
+          tma_load_im2col_4d(base, &map_xhi, c0, w0, h0, n, static_cast<uint16_t>(dx), static_cast<uint16_t>(dy),
+                             &st->b_full[stage]);
+          tma_load_im2col_4d(base + A_PLANE_BYTES, &map_xlo, c0, w0, h0, n, static_cast<uint16_t>(dx),
+                             static_cast<uint16_t>(dy), &st->b_full[stage]);
+          tma_load_2d(base + 2 * A_PLANE_BYTES, &map_whi, kb * BK, 0, &st->b_full[stage]);
+          tma_load_2d(base + 2 * A_PLANE_BYTES + b_plane, &map_wlo, kb * BK, 0, &st->b_full[stage]);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&st->b_full[u % STAGES], (u / STAGES) & 1) && globaltimer_ns() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp < NUM_PRODUCER_WARPS) {
     // ---------------- producers: im2col gather + tf32 split into swizzled smem ----------------
     const int row = (warp & 3) * 32 + lane;     // pixel row of the tile (= A row)
     const int ch0 = (warp >> 2) * 16;           // this warp's 16 channels of the 32-channel block
@@ -202,7 +255,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if (!warp_wait_poll(&st->full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait) ||
+        if ((!TMA_A && !warp_wait_poll(&st->full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait)) ||
             !warp_wait_poll(&st->b_full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait)) {
           ok = false;
           break;
@@ -287,6 +340,30 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// NCHW x -> hi / lo planes in NHWC (channels innermost, as the im2col TMA mode reads them):
+// 32 channels x 32 pixels of one image per block through shared memory, coalesced both ways.
+__global__ void nchw_to_nhwc_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                                          int c, int pix) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
+  const float* xn = x + static_cast<long long>(n) * c * pix;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int ci = c0 + r, pi = p0 + threadIdx.x;
+    tile[r][threadIdx.x] = (ci < c && pi < pix) ? xn[static_cast<long long>(ci) * pix + pi] : 0.0f;
+  }
+  __syncthreads();
+  const long long base = static_cast<long long>(n) * pix * c;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int pi = p0 + r, ci = c0 + threadIdx.x;
+    if (pi < pix && ci < c) {
+      const float v = tile[threadIdx.x][r];
+      const float h = tf32_hi(v);
+      hi[base + static_cast<long long>(pi) * c + ci] = h;
+      lo[base + static_cast<long long>(pi) * c + ci] = v - h;
+    }
+  }
+}
+
 // OIHW weights -> hi / lo planes [OC, kh*kw*C] with the reduction index (dy*kw + dx)*C + c.
 __global__ void conv_weight_split_kernel(const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo,
                                          int oc, int c, int kh, int kw) {
@@ -318,6 +395,43 @@ bool make_weight_map(CUtensorMap* map, const float* base, int rows, int cols) {
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const int*, const int*, cuuint32_t, cuuint32_t,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeIm2colFn im2col_encoder() {
+  static EncodeIm2colFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeIm2colFn>(f);
+  });
+  return fn;
+}
+
+// NHWC fp32 plane [n, h, w, c]: im2col boxes of BM output pixels x BK channels.  The pixel box
+// runs over the output grid: its lower corner is -pad, its upper corner pad - (kernel - 1), and the
+// traversal stride is the conv stride; the per-load offsets select the kernel tap.
+bool make_im2col_map(CUtensorMap* map, const float* base, int n, int h, int w, int c, int kh, int kw, int sh, int sw,
+                     int ph, int pw) {
+  EncodeIm2colFn enc = im2col_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(c), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                        static_cast<cuuint64_t>(n)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(c) * 4, static_cast<cuuint64_t>(w) * c * 4,
+                           static_cast<cuuint64_t>(h) * w * c * 4};
+  int lower[2] = {-pw, -ph};                      // {w, h}
+  int upper[2] = {pw - (kw - 1), ph - (kh - 1)};  // {w, h}
+  cuuint32_t estr[4] = {1, static_cast<cuuint32_t>(sw), static_cast<cuuint32_t>(sh), 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides, lower, upper, BK, BM,
+             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -353,11 +467,33 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
   if (e == cudaSuccess && (!make_weight_map(&mhi, whi, out_c, k) || !make_weight_map(&mlo, wlo, out_c, k)))
     e = cudaErrorInvalidValue;
   const size_t smem = 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * static_cast<size_t>(out_c) * BK * 4) + sizeof(Tail);
+  // The im2col TMA path reads pre-split NHWC planes of x; a small input (< 128 KB) keeps the
+  // gathering producers.
+  const size_t x_elems = static_cast<size_t>(batch) * in_c * in_h * in_w;
+  const bool tma_a = x_elems * 4 >= (size_t(128) << 10) && im2col_encoder() != nullptr && kh <= 128 && kw <= 128 &&
+                     ph <= 127 && pw <= 127 && sh <= 8 && sw <= 8;
+  float* xws = nullptr;
+  CUtensorMap mxhi = mhi, mxlo = mlo;
+  if (e == cudaSuccess && tma_a) {
+    e = workspace_alloc(ctx, reinterpret_cast<void**>(&xws), 2 * x_elems * 4, s);
+    if (e == cudaSuccess) {
+      const int pix = in_h * in_w;
+      nchw_to_nhwc_split_kernel<<<dim3((pix + 31) / 32, (in_c + 31) / 32, batch), dim3(32, 8), 0, s>>>(
+          x, xws, xws + x_elems, in_c, pix);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess && (!make_im2col_map(&mxhi, xws, batch, in_h, in_w, in_c, kh, kw, sh, sw, ph, pw) ||
+                             !make_im2col_map(&mxlo, xws + x_elems, batch, in_h, in_w, in_c, kh, kw, sh, sw, ph, pw)))
+      e = cudaErrorInvalidValue;
+  }
   if (e == cudaSuccess) {
     static bool attr_set = false;  // benign race: idempotent attribute set (largest size once)
     if (!attr_set) {
-      e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
       if (e == cudaSuccess) attr_set = true;
     }
   }
@@ -385,8 +521,15 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
     p.err_word = ctx->err_word;
     const long long tiles = (pixels + BM - 1) / BM;
     const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
-    conv_implicit_tf32x3_kernel<<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, p);
+    if (tma_a)
+      conv_implicit_tf32x3_kernel<true><<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, mxhi, mxlo, p);
+    else
+      conv_implicit_tf32x3_kernel<false><<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, mxhi, mxlo, p);
     e = cudaGetLastError();
+  }
+  if (xws) {
+    const cudaError_t ex = workspace_free(xws, s);
+    if (e == cudaSuccess) e = ex;
   }
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
