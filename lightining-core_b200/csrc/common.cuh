@@ -147,6 +147,28 @@ __device__ __forceinline__ void tma_load_im2col_4d(void* smem_dst, const CUtenso
       : "memory");
 }
 
+// The same im2col load for a CTA pair: completion counted on an mbarrier that may live in the peer
+// CTA (cluster address).  No multicast.
+__device__ __forceinline__ void tma_load_im2col_4d_pair(void* smem_dst, const CUtensorMap* map, int c, int w, int h,
+                                                        int n, uint16_t off_w, uint16_t off_h,
+                                                        uint32_t bar_cluster_addr) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.im2col.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar_cluster_addr), "h"(off_w),
+      "h"(off_h)
+      : "memory");
+}
+// Pair (cta_group::2) tf32 MMA issued from a converged warp by one elected lane.
+__device__ __forceinline__ void umma_tf32_ss_pair_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                    uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 3-D TMA store shared -> global (bulk async-group completion).  Rows outside the tensor map's
 // extent are not written.  The smem writes it reads must precede a fence.proxy.async.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {

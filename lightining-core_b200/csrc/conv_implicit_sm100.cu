@@ -76,12 +76,8 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(u);
 }
 
-// TMA_A: the im2col tiles come from TMA im2col-mode loads of pre-split NHWC planes (map_xhi /
-// map_xlo) issued by one thread, instead of being gathered and split by the producer warps.
-template <bool TMA_A>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     conv_implicit_tf32x3_kernel(const __grid_constant__ CUtensorMap map_whi, const __grid_constant__ CUtensorMap map_wlo,
-                                const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                                 const ConvParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -109,10 +105,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     fence_barrier_init();
     tma_prefetch_desc(&map_whi);
     tma_prefetch_desc(&map_wlo);
-    if (TMA_A) {
-      tma_prefetch_desc(&map_xhi);
-      tma_prefetch_desc(&map_xlo);
-    }
   }
   if (warp == 0) {
     tmem_alloc(&st->tmem_base, TMEM_COLS);
@@ -124,50 +116,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
 
-  if (TMA_A && warp < NUM_PRODUCER_WARPS) {
-    // ---------------- one thread: TMA im2col loads of the A planes + the weight planes --------
-    if (warp == 0 && lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        // The tile's first output pixel: (n, oy, ox) -> input coordinates of its top-left tap.
-        const int gp = t * BM;
-        const int n = gp / pix_img, pp = gp - n * pix_img;
-        const int oy = pp / p.ow, ox = pp - oy * p.ow;
-        const int w0 = ox * p.sw - p.pw, h0 = oy * p.sh - p.ph;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, p.err_word, kErrGemmProducerWait)) {
-            ok = false;
-            break;
-          }
-          uint8_t* base = smem + stage * stage_bytes;
-          const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * BK;
-          const int dy = tap / p.kw, dx = tap - dy * p.kw;
-          mbar_arrive_expect_tx(&st->b_full[stage], 2 * A_PLANE_BYTES + 2 * b_plane);
-          tma_load_im2col_4d(base, &map_xhi, c0, w0, h0, n, static_cast<uint16_t>(dx), static_cast<uint16_t>(dy),
-                             &st->b_full[stage]);
-          tma_load_im2col_4d(base + A_PLANE_BYTES, &map_xlo, c0, w0, h0, n, static_cast<uint16_t>(dx),
-                             static_cast<uint16_t>(dy), &st->b_full[stage]);
-          tma_load_2d(base + 2 * A_PLANE_BYTES, &map_whi, kb * BK, 0, &st->b_full[stage]);
-          tma_load_2d(base + 2 * A_PLANE_BYTES + b_plane, &map_wlo, kb * BK, 0, &st->b_full[stage]);
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-      if (!ok) {
-        for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
-          const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(&st->b_full[u % STAGES], (u / STAGES) & 1) && globaltimer_ns() - t0 < 100000000ull) {
-          }
-        }
-      }
-    }
-  } else if (warp < NUM_PRODUCER_WARPS) {
+  if (warp < NUM_PRODUCER_WARPS) {
     // ---------------- producers: im2col gather + tf32 split into swizzled smem ----------------
     const int row = (warp & 3) * 32 + lane;     // pixel row of the tile (= A row)
     const int ch0 = (warp >> 2) * 16;           // this warp's 16 channels of the 32-channel block
@@ -255,7 +204,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
       for (int kb = 0; kb < p.num_kb; ++kb) {
-        if ((!TMA_A && !warp_wait_poll(&st->full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait)) ||
+        if (!warp_wait_poll(&st->full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait) ||
             !warp_wait_poll(&st->b_full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait)) {
           ok = false;
           break;
@@ -340,6 +289,231 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---- cluster-pair kernel fed by TMA im2col loads -----------------------------------------------
+// Two CTAs (two SMs) compute a 256-pixel tile with tcgen05.mma.cta_group::2 (M = 256, N = OC):
+// each CTA TMA-loads the im2col planes of its own 128 pixels and half of the weight rows, so a
+// stage is 32 KB + OC x 128 B (56 KB at OC = 192) and up to four stages fit.  The leader CTA arms
+// each stage for both CTAs' bytes and issues every MMA; its commits release the stage in both CTAs
+// and hand each CTA's accumulator lanes to that CTA's epilogue, which releases it with a remote
+// arrival on the leader.  192 threads: warp 0 TMA, warp 1 MMA (leader), warps 2..5 epilogue.
+namespace pairk {
+constexpr int MAX_STAGES = 4;
+constexpr int NUM_THREADS = 192;
+constexpr size_t SMEM_LIMIT = 232448;  // opt-in shared memory per block on sm_100
+struct Tail {
+  uint64_t full[MAX_STAGES];    // leader: both CTAs' bytes of the stage landed
+  uint64_t empty[MAX_STAGES];   // per CTA: the leader's MMAs reading this stage finished
+  uint64_t tmem_full[2];        // per CTA: its lanes of a tile's accumulator are final
+  uint64_t tmem_empty[2];       // leader: the 8 epilogue warps of both CTAs drained it
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+size_t stage_bytes(int out_c) { return 2 * A_PLANE_BYTES + static_cast<size_t>(out_c) * BK * 4; }
+int stages(int out_c) {
+  const int st = static_cast<int>((SMEM_LIMIT - 1024 - sizeof(Tail)) / stage_bytes(out_c));
+  return st < MAX_STAGES ? st : MAX_STAGES;
+}
+}  // namespace pairk
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::NUM_THREADS, 1)
+    conv_im2col_pair_kernel(const __grid_constant__ CUtensorMap map_whi, const __grid_constant__ CUtensorMap map_wlo,
+                            const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                            const ConvParams p, int nstages) {
+  using pairk::Tail;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // Both CTAs compute the same aligned offsets (the MMA descriptors name one offset for both).
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int half_oc = p.out_c / 2;
+  const int b_plane = half_oc * BK * 4;                     // this CTA's weight rows, one plane
+  const int sbytes = 2 * A_PLANE_BYTES + 2 * b_plane;       // A_hi | A_lo | W_hi | W_lo
+  const int STAGES = nstages;
+  Tail* st = reinterpret_cast<Tail*>(smem + STAGES * sbytes);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = static_cast<int>(blockIdx.x) >> 1;
+  const int num_clusters = static_cast<int>(gridDim.x) >> 1;
+  const int num_tiles = (p.pixels + 2 * BM - 1) / (2 * BM);
+  const int cblocks = p.in_c / BK;
+  const int pix_img = p.oh * p.ow;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&st->tmem_full[b], 1);
+      mbar_init(&st->tmem_empty[b], 8);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init_cluster();
+    tma_prefetch_desc(&map_whi);
+    tma_prefetch_desc(&map_wlo);
+    tma_prefetch_desc(&map_xhi);
+    tma_prefetch_desc(&map_xlo);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barrier inits and the TMEM allocation visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        const int gp = t * 2 * BM + static_cast<int>(rank) * BM;  // this CTA's first pixel
+        const int n = gp / pix_img, pp = gp - n * pix_img;
+        const int oy = pp / p.ow, ox = pp - oy * p.ow;
+        const int w0 = ox * p.sw - p.pw, h0 = oy * p.sh - p.ph;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          // empty[stage] (this CTA's) next completes for the use after this one, which needs the
+          // loads issued here: the parity wait is unambiguous.
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, p.err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&st->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&st->full[stage], 2 * sbytes);
+          uint8_t* base = smem + stage * sbytes;
+          const int tap = kb / cblocks, c0 = (kb - tap * cblocks) * BK;
+          const uint16_t dy = static_cast<uint16_t>(tap / p.kw), dx = static_cast<uint16_t>(tap % p.kw);
+          tma_load_im2col_4d_pair(base, &map_xhi, c0, w0, h0, n, dx, dy, full_leader);
+          tma_load_im2col_4d_pair(base + A_PLANE_BYTES, &map_xlo, c0, w0, h0, n, dx, dy, full_leader);
+          const int wrow = static_cast<int>(rank) * half_oc;
+          tma_load_2d_pair(base + 2 * A_PLANE_BYTES, &map_whi, kb * BK, wrow, full_leader);
+          tma_load_2d_pair(base + 2 * A_PLANE_BYTES + b_plane, &map_wlo, kb * BK, wrow, full_leader);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: the leader's last commits on this CTA's empty barriers (so every MMA read of this
+      // CTA's stages) must land before the CTA may exit.  Use u of a stage: phase u / STAGES.
+      for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->empty[u % STAGES], (u / STAGES) & 1) && !*abort_flag &&
+               globaltimer_ns() - t0 < 200000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader CTA only) ----------------
+    if (leader) {
+      const uint32_t idesc = idesc_tf32_f32(2 * BM, p.out_c, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, p.err_word, kErrGemmMmaWait)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!warp_wait_poll(&st->full[stage], phase, abort_flag, p.err_word, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + stage * sbytes);
+          const uint64_t ahd = smem_desc_sw128(a_hi, 16, 1024);
+          const uint64_t ald = smem_desc_sw128(a_hi + A_PLANE_BYTES, 16, 1024);
+          const uint64_t bhd = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES, 16, 1024);
+          const uint64_t bld = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES + b_plane, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            // K-major SW128 operands: rows 128 B apart, 8-row groups 1 KB apart; +32 B per K=8 step.
+            const uint32_t first = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_tf32_ss_pair_w(d_tmem, ald + k * 2, bhd + k * 2, idesc, first);
+            umma_tf32_ss_pair_w(d_tmem, ahd + k * 2, bld + k * 2, idesc, 1u);
+            umma_tf32_ss_pair_w(d_tmem, ahd + k * 2, bhd + k * 2, idesc, 1u);
+            issued = true;
+          }
+          umma_commit_pair_w(&st->empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_w(&st->tmem_full[acc], 0x3);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_pair_w(&st->drain, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs): TMEM -> bias -> ReLU -> NCHW ----------
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      if (!warp_wait_poll(&st->tmem_full[acc], acc_phase, abort_flag, p.err_word, kErrGemmEpilogueWait)) break;
+      tc_fence_after();
+      const int gp = t * 2 * BM + static_cast<int>(rank) * BM + row;
+      const bool pix_ok = gp < p.pixels;
+      const int n = pix_ok ? gp / pix_img : 0;
+      const int pp = gp - n * pix_img;
+      float* dst = p.out + static_cast<long long>(n) * p.out_c * pix_img + pp;
+      const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * 256) + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < p.out_c; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld16(tbase + c0, r);
+        if (pix_ok) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v = __uint_as_float(r[j]) + (p.bias ? __ldg(p.bias + c0 + j) : 0.0f);
+            if (p.relu) v = fmaxf(v, 0.0f);
+            dst[static_cast<long long>(c0 + j) * pix_img] = v;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&st->tmem_empty[acc]), 0));
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs, commits or arrivals can touch it
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 // NCHW x -> hi / lo planes in NHWC (channels innermost, as the im2col TMA mode reads them):
 // 32 channels x 32 pixels of one image per block through shared memory, coalesced both ways.
 __global__ void nchw_to_nhwc_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
@@ -385,13 +559,13 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// [rows, cols] fp32 row-major, box [rows, 32 columns], 128-byte swizzle.
-bool make_weight_map(CUtensorMap* map, const float* base, int rows, int cols) {
+// [rows, cols] fp32 row-major, box [box_rows, 32 columns], 128-byte swizzle.
+bool make_weight_map(CUtensorMap* map, const float* base, int rows, int cols, int box_rows) {
   auto enc = reinterpret_cast<EncodeTiledFn>(tensor_map_encoder());
   if (!enc) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
-  cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(rows)};
+  cuuint32_t box[2] = {BK, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -463,17 +637,16 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
     conv_weight_split_kernel<<<blocks, 256, 0, s>>>(w, whi, wlo, out_c, in_c, kh, kw);
     e = cudaGetLastError();
   }
-  CUtensorMap mhi, mlo;
-  if (e == cudaSuccess && (!make_weight_map(&mhi, whi, out_c, k) || !make_weight_map(&mlo, wlo, out_c, k)))
-    e = cudaErrorInvalidValue;
-  const size_t smem = 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * static_cast<size_t>(out_c) * BK * 4) + sizeof(Tail);
-  // The im2col TMA path reads pre-split NHWC planes of x; a small input (< 128 KB) keeps the
-  // gathering producers.
+  // The im2col TMA path (a CTA pair per 256-pixel tile) reads pre-split NHWC planes of x; a small
+  // input (< 128 KB) keeps the 1-CTA kernel with gathering producers.
   const size_t x_elems = static_cast<size_t>(batch) * in_c * in_h * in_w;
   const bool tma_a = x_elems * 4 >= (size_t(128) << 10) && im2col_encoder() != nullptr && kh <= 128 && kw <= 128 &&
-                     ph <= 127 && pw <= 127 && sh <= 8 && sw <= 8;
+                     ph <= 127 && pw <= 127 && sh <= 8 && sw <= 8 && ctx->sm_count >= 2;
+  CUtensorMap mhi, mlo, mxhi, mxlo;
+  const int wbox = tma_a ? out_c / 2 : out_c;
+  if (e == cudaSuccess && (!make_weight_map(&mhi, whi, out_c, k, wbox) || !make_weight_map(&mlo, wlo, out_c, k, wbox)))
+    e = cudaErrorInvalidValue;
   float* xws = nullptr;
-  CUtensorMap mxhi = mhi, mxlo = mlo;
   if (e == cudaSuccess && tma_a) {
     e = workspace_alloc(ctx, reinterpret_cast<void**>(&xws), 2 * x_elems * 4, s);
     if (e == cudaSuccess) {
@@ -489,11 +662,11 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
   if (e == cudaSuccess) {
     static bool attr_set = false;  // benign race: idempotent attribute set (largest size once)
     if (!attr_set) {
-      e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
       if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
+        e = cudaFuncSetAttribute(conv_im2col_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(pairk::SMEM_LIMIT));
       if (e == cudaSuccess) attr_set = true;
     }
   }
@@ -519,12 +692,19 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
     p.pixels = static_cast<int>(pixels);
     p.num_kb = k / BK;
     p.err_word = ctx->err_word;
-    const long long tiles = (pixels + BM - 1) / BM;
-    const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
-    if (tma_a)
-      conv_implicit_tf32x3_kernel<true><<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, mxhi, mxlo, p);
-    else
-      conv_implicit_tf32x3_kernel<false><<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, mxhi, mxlo, p);
+    if (tma_a) {
+      const int nst = pairk::stages(out_c);
+      const size_t psmem = 1024 + nst * pairk::stage_bytes(out_c) + sizeof(pairk::Tail);
+      const long long tiles = (pixels + 2 * BM - 1) / (2 * BM);
+      const int max_clusters = ctx->sm_count / 2;
+      const int clusters = static_cast<int>(tiles < max_clusters ? tiles : max_clusters);
+      conv_im2col_pair_kernel<<<2 * clusters, pairk::NUM_THREADS, psmem, s>>>(mhi, mlo, mxhi, mxlo, p, nst);
+    } else {
+      const long long tiles = (pixels + BM - 1) / BM;
+      const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
+      const size_t smem = 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * static_cast<size_t>(out_c) * BK * 4) + sizeof(Tail);
+      conv_implicit_tf32x3_kernel<<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, p);
+    }
     e = cudaGetLastError();
   }
   if (xws) {
