@@ -575,7 +575,20 @@ bool attention_f32_tc_supported(const AttnArgs& a) {
 }
 
 cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, size_t nv, int sp, DeviceCtx* ctx,
-                                    cudaStream_t s);
+                                    cudaStream_t s, bool qk_ready);
+
+size_t attention_f32_tc_ws_floats(int units, int seq) {
+  const int sp = (seq + 3) & ~3;
+  return 4 * static_cast<size_t>(units) * seq * D + 2 * static_cast<size_t>(units) * D * sp;
+}
+
+cudaError_t attention_f32_tc_presplit_qk(const AttnArgs& a, float* ws, cudaStream_t s) {
+  DeviceCtx* ctx = device_ctx();
+  if (!ctx) return cudaErrorNoDevice;
+  const int sp = (a.seq + 3) & ~3;
+  const size_t nqk = static_cast<size_t>(a.units) * a.seq * D, nv = static_cast<size_t>(a.units) * D * sp;
+  return attention_f32_tc_planes(a, ws, nqk, nv, sp, ctx, s, true);
+}
 
 cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
@@ -588,13 +601,13 @@ cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s) {
   float* ws = nullptr;
   cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws), bytes, s);
   if (e != cudaSuccess) return e;
-  e = attention_f32_tc_planes(a, ws, nqk, nv, sp, ctx, s);
+  e = attention_f32_tc_planes(a, ws, nqk, nv, sp, ctx, s, false);
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
 }
 
 cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, size_t nv, int sp, DeviceCtx* ctx,
-                                    cudaStream_t s) {
+                                    cudaStream_t s, bool qk_ready) {
   cudaError_t e = cudaSuccess;
   float* qh = ws;
   float* ql = qh + nqk;
@@ -616,8 +629,10 @@ cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, si
   }
   const dim3 sgrid(static_cast<unsigned>(std::min<long long>((static_cast<long long>(a.seq) * D / 4 + 255) / 256, 64)),
                    static_cast<unsigned>(a.units));
-  split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.seq);
-  split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.seq);
+  if (!qk_ready) {
+    split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.seq);
+    split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.seq);
+  }
   split_vt_kernel<<<dim3((sp + 31) / 32, D / 32, a.units), dim3(32, 8), 0, s>>>(static_cast<const float*>(a.v),
                                                                                 a.v_unit_stride, vh, vl, a.seq, sp);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;

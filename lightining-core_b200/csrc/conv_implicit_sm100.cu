@@ -67,6 +67,7 @@ struct ConvParams {
   int pixels;  // batch * oh * ow
   int num_kb;  // kh * kw * in_c / BK
   unsigned* err_word;
+  QkvSplitOut qkv;  // fused integrated-pipeline epilogue (cluster-pair kernel only) when qkv.q_hi != nullptr
 };
 
 // x rounded to tf32 (nearest, ties away), the 13 low mantissa bits cleared; inf/NaN pass through.
@@ -480,18 +481,55 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::NUM_THREADS, 
       const bool pix_ok = gp < p.pixels;
       const int n = pix_ok ? gp / pix_img : 0;
       const int pp = gp - n * pix_img;
-      float* dst = p.out + static_cast<long long>(n) * p.out_c * pix_img + pp;
       const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * 256) + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (!p.qkv.q_hi) {
+        float* dst = p.out + static_cast<long long>(n) * p.out_c * pix_img + pp;
 #pragma unroll 1
-      for (int c0 = 0; c0 < p.out_c; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(tbase + c0, r);
-        if (pix_ok) {
+        for (int c0 = 0; c0 < p.out_c; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
+          if (pix_ok) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float v = __uint_as_float(r[j]) + (p.bias ? __ldg(p.bias + c0 + j) : 0.0f);
-            if (p.relu) v = fmaxf(v, 0.0f);
-            dst[static_cast<long long>(c0 + j) * pix_img] = v;
+            for (int j = 0; j < 16; ++j) {
+              float v = __uint_as_float(r[j]) + (p.bias ? __ldg(p.bias + c0 + j) : 0.0f);
+              if (p.relu) v = fmaxf(v, 0.0f);
+              dst[static_cast<long long>(c0 + j) * pix_img] = v;
+            }
+          }
+        }
+      } else {
+        // Fused pipeline: channel c of image n is flat range [c*pix, (c+1)*pix) of the image's conv
+        // output; with need a multiple of pix, channels [0, cpn) are Q, [cpn, 2cpn) K, [2cpn, 3cpn) V
+        // (cpn a multiple of 16 here, so a 16-channel group lies in one operand).
+        const int cpn = static_cast<int>(p.qkv.need / pix_img);
+        const long long rowoff = static_cast<long long>(n) * p.qkv.need + pp;
+#pragma unroll 1
+        for (int c0 = 0; c0 < p.out_c && c0 < 3 * cpn; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c0, r);
+          const int seg = (c0 >= cpn) + (c0 >= 2 * cpn);
+          const long long o = rowoff + static_cast<long long>(c0 - seg * cpn) * pix_img;
+          if (pix_ok) {
+            if (seg == 2) {
+              float* d = p.qkv.v + o;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                float v = __uint_as_float(r[j]) + (p.bias ? __ldg(p.bias + c0 + j) : 0.0f);
+                if (p.relu) v = fmaxf(v, 0.0f);
+                d[static_cast<long long>(j) * pix_img] = v;
+              }
+            } else {
+              float* dh = (seg ? p.qkv.k_hi : p.qkv.q_hi) + o;
+              float* dl = (seg ? p.qkv.k_lo : p.qkv.q_lo) + o;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                float v = __uint_as_float(r[j]) + (p.bias ? __ldg(p.bias + c0 + j) : 0.0f);
+                if (p.relu) v = fmaxf(v, 0.0f);
+                const float h = tf32_hi(v);
+                dh[static_cast<long long>(j) * pix_img] = h;
+                dl[static_cast<long long>(j) * pix_img] = v - h;
+              }
+            }
           }
         }
       }
@@ -616,9 +654,43 @@ bool conv_implicit_supported(int in_c, int out_c, int kh, int kw) {
          static_cast<long long>(in_c) * kh * kw < (1LL << 24) && tensor_map_encoder() != nullptr;
 }
 
+namespace {
+// The cluster-pair TMA-im2col path takes the shape (the input is large enough for the im2col tensor
+// map, the kernel geometry fits its corner and stride ranges).
+bool pair_path_ok(size_t x_elems, int kh, int kw, int sh, int sw, int ph, int pw) {
+  return x_elems * 4 >= (size_t(128) << 10) && im2col_encoder() != nullptr && kh <= 128 && kw <= 128 && ph <= 127 &&
+         pw <= 127 && sh <= 8 && sw <= 8;
+}
+
+cudaError_t conv_implicit_run(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                              int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
+                              const QkvSplitOut* qkv, cudaStream_t s);
+}  // namespace
+
+bool conv_qkv_split_supported(int batch, int in_c, int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw,
+                              int ph, int pw) {
+  (void)sh, (void)sw;
+  return conv_implicit_supported(in_c, out_c, kh, kw) &&
+         pair_path_ok(static_cast<size_t>(batch) * in_c * in_h * in_w, kh, kw, sh, sw, ph, pw);
+}
+
+cudaError_t conv2d_nchw_f32_implicit_qkv(const float* x, const float* w, const float* bias, int batch, int in_c,
+                                         int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph,
+                                         int pw, int relu, const QkvSplitOut& qkv, cudaStream_t s) {
+  if (!conv_qkv_split_supported(batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw)) return cudaErrorNotSupported;
+  return conv_implicit_run(x, w, bias, nullptr, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, &qkv, s);
+}
+
 cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float* bias, float* out, int batch,
                                      int in_c, int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph,
                                      int pw, int relu, cudaStream_t s) {
+  return conv_implicit_run(x, w, bias, out, batch, in_c, in_h, in_w, out_c, kh, kw, sh, sw, ph, pw, relu, nullptr, s);
+}
+
+namespace {
+cudaError_t conv_implicit_run(const float* x, const float* w, const float* bias, float* out, int batch, int in_c,
+                              int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph, int pw, int relu,
+                              const QkvSplitOut* qkv, cudaStream_t s) {
   if (!conv_implicit_supported(in_c, out_c, kh, kw)) return cudaErrorNotSupported;
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
@@ -640,8 +712,11 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
   // The im2col TMA path (a CTA pair per 256-pixel tile) reads pre-split NHWC planes of x; a small
   // input (< 128 KB) keeps the 1-CTA kernel with gathering producers.
   const size_t x_elems = static_cast<size_t>(batch) * in_c * in_h * in_w;
-  const bool tma_a = x_elems * 4 >= (size_t(128) << 10) && im2col_encoder() != nullptr && kh <= 128 && kw <= 128 &&
-                     ph <= 127 && pw <= 127 && sh <= 8 && sw <= 8 && ctx->sm_count >= 2;
+  const bool tma_a = pair_path_ok(x_elems, kh, kw, sh, sw, ph, pw) && ctx->sm_count >= 2;
+  if (qkv && !tma_a) {
+    workspace_free(ws, s);
+    return cudaErrorNotSupported;
+  }
   CUtensorMap mhi, mlo, mxhi, mxlo;
   const int wbox = tma_a ? out_c / 2 : out_c;
   if (e == cudaSuccess && (!make_weight_map(&mhi, whi, out_c, k, wbox) || !make_weight_map(&mlo, wlo, out_c, k, wbox)))
@@ -692,6 +767,7 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
     p.pixels = static_cast<int>(pixels);
     p.num_kb = k / BK;
     p.err_word = ctx->err_word;
+    p.qkv = qkv ? *qkv : QkvSplitOut{nullptr, nullptr, nullptr, nullptr, nullptr, 0};
     if (tma_a) {
       const int nst = pairk::stages(out_c);
       const size_t psmem = 1024 + nst * pairk::stage_bytes(out_c) + sizeof(pairk::Tail);
@@ -714,5 +790,7 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
 }
+
+}  // namespace
 
 }  // namespace lcb

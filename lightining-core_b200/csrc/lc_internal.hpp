@@ -97,6 +97,21 @@ cudaError_t conv2d_nchw_f32_implicit(const float* x, const float* w, const float
                                      int in_c, int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph,
                                      int pw, int relu, cudaStream_t s);
 constexpr const char* kConvImplicitName = "tcgen05_implicit";
+// The integrated pipeline's fused conv epilogue: instead of the NCHW output, each image's flat conv
+// output f (= c * OH*OW + pixel) goes to the attention's operands directly -- f < need: Q hi/lo
+// planes, need <= f < 2*need: K hi/lo planes (tf32 split, [images, seq, head_dim] contiguous),
+// 2*need <= f < 3*need: V unsplit ([images, need]); the rest is unused by the attention.  need must
+// be a multiple of OH*OW (whole channels per operand).
+struct QkvSplitOut {
+  float *q_hi, *q_lo, *k_hi, *k_lo, *v;
+  long long need;  // seq * head_dim
+};
+// True when conv2d_nchw_f32_implicit can write the fused QKV planes for this shape.
+bool conv_qkv_split_supported(int batch, int in_c, int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw,
+                              int ph, int pw);
+cudaError_t conv2d_nchw_f32_implicit_qkv(const float* x, const float* w, const float* bias, int batch, int in_c,
+                                         int in_h, int in_w, int out_c, int kh, int kw, int sh, int sw, int ph,
+                                         int pw, int relu, const QkvSplitOut& qkv, cudaStream_t s);
 // Cyclic repeat of the first `have` floats of src into dst[0, total) (qkv_pack short case).
 cudaError_t repeat_fill_f32(const float* src, size_t have, float* dst, size_t total, cudaStream_t s);
 
@@ -121,6 +136,11 @@ cudaError_t attention_f32_simt(const AttnArgs& a, cudaStream_t s);
 // Strict fp32 attention on tcgen05 by the 3xTF32 split (attention_tf32x3.cu), head_dim 64.
 bool attention_f32_tc_supported(const AttnArgs& a);
 cudaError_t attention_f32_tc(const AttnArgs& a, cudaStream_t s);
+// The 3xTF32 attention on a caller-provided plane workspace [Q_hi | Q_lo | K_hi | K_lo | V^T_hi |
+// V^T_lo] (attention_f32_tc_ws_floats) whose Q and K planes are already filled (the fused conv
+// epilogue writes them); a.v is the unsplit V.  Same kernel and results as attention_f32_tc.
+size_t attention_f32_tc_ws_floats(int units, int seq);
+cudaError_t attention_f32_tc_presplit_qk(const AttnArgs& a, float* ws, cudaStream_t s);
 // Train step pieces (fp32): dO = 2(O - T)/(seq*d) and per-unit sum of squared errors (double);
 // then dV = P^T dO recomputed from Q, K and the forward's LSE, applied as v -= lr * dV in place.
 cudaError_t attention_train_grad_out(const float* out, const float* target, float* dout, double* sse, int units,

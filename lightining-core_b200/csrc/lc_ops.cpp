@@ -8,6 +8,7 @@
 #include <climits>
 #include <cmath>
 #include <cstring>
+#include <string>
 #include <vector>
 
 #include "lc_host.hpp"
@@ -593,6 +594,68 @@ lcError_t lcConvAttentionNchw(const float* x, const float* w, const float* bias,
   LC_TRY(io.scratch(batch * img * 4, &conv));
   cudaStream_t s = io.stream();
   trace_op(kOpConv2dNchw, batch * oh * ow * out_channels * in_channels * kernel_h * kernel_w);
+  {
+    // Fused route (per-image semantics, conv output long enough, head_dim 64, strict-fp32 tensor-core
+    // attention, cluster-pair conv): the conv epilogue writes the attention's Q / K tf32 hi-lo
+    // planes and the unsplit V directly, so the QKV tensor never exists as a separate NCHW buffer
+    // and no split pass runs over Q and K.  Skipped when a tune-cache entry pins another kernel.
+    const size_t avail_img = img;
+    AttnArgs a{};
+    a.units = static_cast<int>(units);
+    a.seq = static_cast<int>(seq);
+    a.d = static_cast<int>(head_dim);
+    a.causal = 0;
+    a.scale = 1.0f / sqrtf(static_cast<float>(head_dim));
+    a.post_scale = 1.0f;
+    a.post_bias = 0.0f;
+    a.post_relu = 0;
+    a.proj_w = static_cast<const float*>(dp);
+    a.proj_cols = static_cast<int>(proj_cols);
+    a.out = dout;
+    a.out_unit_stride = static_cast<long long>(seq * cols);
+    std::string cfg;
+    size_t k0, k1, k2;
+    const bool conv_pinned =
+        conv_tune_key(batch, in_channels, in_h, in_w, out_channels, kernel_h, kernel_w, stride_h, stride_w, pad_h,
+                      pad_w, &k0, &k1, &k2) &&
+        tune_lookup(LC_TUNE_CONV, k0, k1, k2, LC_DTYPE_F32, &cfg) && cfg != kConvImplicitName;
+    const bool attn_pinned = tune_lookup(LC_TUNE_ATTENTION, seq, head_dim, 0, LC_DTYPE_F32, &cfg) && cfg == "simt";
+    const long long macs = static_cast<long long>(batch * oh * ow) * out_channels * in_channels * kernel_h * kernel_w;
+    if ((per_image || batch == 1) && avail_img >= 3 * need && need % (16 * oh * ow) == 0 && need <= (size_t)INT_MAX &&
+        head_dim == 64 && units <= 65535 && !conv_pinned &&
+        !attn_pinned && macs >= (1LL << 26) &&
+        conv_qkv_split_supported((int)batch, (int)in_channels, (int)in_h, (int)in_w, (int)out_channels,
+                                 (int)kernel_h, (int)kernel_w, (int)stride_h, (int)stride_w, (int)pad_h,
+                                 (int)pad_w)) {
+      a.q_unit_stride = a.k_unit_stride = a.v_unit_stride = static_cast<long long>(need);
+      // Plane layout of the attention: [Q_hi | Q_lo | K_hi | K_lo | V^T_hi | V^T_lo], then the raw V.
+      const size_t nqk = units * need;
+      a.q = a.k = nullptr;  // read from the planes
+      if (attention_f32_tc_supported(a)) {
+        DeviceCtx* ctx = device_ctx();
+        if (!ctx) return LC_NOT_INITIALIZED;
+        const size_t ws_floats = attention_f32_tc_ws_floats((int)units, (int)seq) + nqk;
+        float* ws = nullptr;
+        LC_TRY(workspace_alloc(ctx, reinterpret_cast<void**>(&ws), ws_floats * 4, s));
+        float* vraw = ws + attention_f32_tc_ws_floats((int)units, (int)seq);
+        const QkvSplitOut qkv{ws, ws + nqk, ws + 2 * nqk, ws + 3 * nqk, vraw, static_cast<long long>(need)};
+        a.v = vraw;
+        cudaError_t e = conv2d_nchw_f32_implicit_qkv(
+            static_cast<const float*>(dx), static_cast<const float*>(dw), static_cast<const float*>(db), (int)batch,
+            (int)in_channels, (int)in_h, (int)in_w, (int)out_channels, (int)kernel_h, (int)kernel_w, (int)stride_h,
+            (int)stride_w, (int)pad_h, (int)pad_w, 1, qkv, s);
+        if (e == cudaSuccess) {
+          trace_op(kOpAttention, units * seq * seq * head_dim);
+          e = attention_f32_tc_presplit_qk(a, ws, s);
+        }
+        const cudaError_t ef = workspace_free(ws, s);
+        LC_TRY(e);
+        LC_TRY(ef);
+        LC_TRY(io.finish(out, dout, out_bytes, pol.download_out, pol.synchronize));
+        return check_error_word(pol.synchronize || pol.download_out);
+      }
+    }
+  }
   // Conv + bias + ReLU; its NCHW output already is the QKV arrangement (raw channel-block slices).
   LC_TRY(conv2d_nchw_f32(static_cast<const float*>(dx), static_cast<const float*>(dw), static_cast<const float*>(db),
                          static_cast<float*>(conv), (int)batch, (int)in_channels, (int)in_h, (int)in_w,
