@@ -9,7 +9,8 @@
 // hi/lo planes of B^T [N,K], so both operands are K-major in shared memory.  The GEMM is
 // persistent, one CTA per SM, 192 threads: warp 0 TMA (A planes 128x32, B^T planes 128x32,
 // 128-byte swizzle, 3-stage ring of 64 KB), warp 1 one thread issuing tcgen05.mma.kind::tf32
-// (M=128, N=128, K=8) three times per K step, warps 2..5 the epilogue.
+// (M=128, N=128, K=8) three times per K step, warps 2..5 the epilogue.  The matmul runs the
+// cluster-pair variant (M=256 per CTA pair, 4-stage ring); the im2col conv the one-CTA kernel.
 // Accuracy: the tensor core's fp32 accumulation over thousands of terms drifts by up to ~1e-3
 // (it does not round like a sequential fp32 sum), so the MMAs only accumulate 128-deep K chunks,
 // each into one of four rotating 128-column TMEM buffers, and the epilogue warps add the chunks
@@ -429,6 +430,258 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
+// ---- cluster-pair variant ---------------------------------------------------------------------
+// Two CTAs (two SMs) compute a 256 x BN tile with tcgen05.mma.cta_group::2.kind::tf32 (M = 256,
+// N = BN, K = 8): each CTA stages its own 128 rows of the A planes and half of the B^T rows, so a
+// stage is 32 KB + BN x 128 B and four stages fit; the leader issues every MMA, its commits release
+// the stage in both CTAs and hand each CTA its accumulator lanes chunk by chunk; each CTA's
+// epilogue folds its rows' chunks into fp32 registers exactly as the one-CTA kernel does.
+namespace pairg {
+constexpr int STAGES = 4;
+constexpr int NUM_THREADS = 192;
+struct Tail {
+  uint64_t full[STAGES];          // leader: both CTAs' bytes of the stage landed
+  uint64_t empty[STAGES];         // per CTA: the leader's MMAs reading this stage finished
+  uint64_t tmem_full[ACC_BUFS];   // per CTA: its lanes of a K chunk's partial sum are in buffer b
+  uint64_t tmem_empty[ACC_BUFS];  // leader: the 8 epilogue warps of both CTAs folded buffer b
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t smem_bytes(int bn) { return 1024 + STAGES * (2 * A_PLANE_BYTES + bn * BK * 4) + sizeof(Tail); }
+}  // namespace pairg
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 1)
+    gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                            const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+                            float* __restrict__ C, int M, int N, int K, int period, long long batch_stride,
+                            long long row_stride, const float* __restrict__ row_bias, int relu, unsigned* err_word) {
+  using pairg::Tail;
+  constexpr int STAGES = pairg::STAGES;
+  constexpr int B_HALF_PLANE = (BN / 2) * BK * 4;
+  constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * B_HALF_PLANE;  // A_hi | A_lo | B_hi | B_lo (this CTA's half)
+  constexpr uint32_t IDESC = idesc_tf32_f32(2 * BM, BN, 0, 0);
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Tail* st = reinterpret_cast<Tail*>(smem + STAGES * STAGE_BYTES);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = static_cast<int>(blockIdx.x) >> 1;
+  const int num_clusters = static_cast<int>(gridDim.x) >> 1;
+  const int tiles_m = (M + 2 * BM - 1) / (2 * BM);
+  const int tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    for (int b = 0; b < ACC_BUFS; ++b) {
+      mbar_init(&st->tmem_full[b], 1);
+      mbar_init(&st->tmem_empty[b], 8);
+    }
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    fence_barrier_init_cluster();
+    tma_prefetch_desc(&map_ahi);
+    tma_prefetch_desc(&map_alo);
+    tma_prefetch_desc(&map_bhi);
+    tma_prefetch_desc(&map_blo);
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(&st->tmem_base, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barrier inits and the TMEM allocation visible to both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        int mb, nb;
+        tile_coords(t, tiles_m, tiles_n, mb, nb);
+        const int row0 = mb * 2 * BM + static_cast<int>(rank) * BM;
+        const int col0 = nb * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&st->full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&st->full[stage], 2 * STAGE_BYTES);
+          uint8_t* base = smem + stage * STAGE_BYTES;
+          tma_load_2d_pair(base, &map_ahi, kb * BK, row0, full_leader);
+          tma_load_2d_pair(base + A_PLANE_BYTES, &map_alo, kb * BK, row0, full_leader);
+          tma_load_2d_pair(base + 2 * A_PLANE_BYTES, &map_bhi, kb * BK, col0, full_leader);
+          tma_load_2d_pair(base + 2 * A_PLANE_BYTES + B_HALF_PLANE, &map_blo, kb * BK, col0, full_leader);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: the leader's last commits on this CTA's empty barriers must land before exit.
+      for (int u = issued > STAGES ? issued - STAGES : 0; u < issued; ++u) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->empty[u % STAGES], (u / STAGES) & 1) && !*abort_flag &&
+               globaltimer_ns() - t0 < 200000000ull) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader only) ----------------
+    if (leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, issued = false;
+      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+        uint32_t d_tmem = tmem_base;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          const int kc = kb % CHUNK_KB;
+          if (kc == 0) {
+            if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+          }
+          if (!warp_wait_poll(&st->full[stage], phase, abort_flag, err_word, kErrGemmMmaWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_hi = smem_u32(smem + stage * STAGE_BYTES);
+          const uint64_t ahd0 = smem_desc_sw128(a_hi, 16, 1024);
+          const uint64_t ald0 = smem_desc_sw128(a_hi + A_PLANE_BYTES, 16, 1024);
+          const uint64_t bhd0 = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES, 16, 1024);
+          const uint64_t bld0 = smem_desc_sw128(a_hi + 2 * A_PLANE_BYTES + B_HALF_PLANE, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint32_t first = (kc > 0 || k > 0) ? 1u : 0u;
+            umma_tf32_ss_pair_w(d_tmem, ald0 + k * 2, bhd0 + k * 2, IDESC, first);  // small terms first
+            umma_tf32_ss_pair_w(d_tmem, ahd0 + k * 2, bld0 + k * 2, IDESC, 1u);
+            umma_tf32_ss_pair_w(d_tmem, ahd0 + k * 2, bhd0 + k * 2, IDESC, 1u);
+            issued = true;
+          }
+          umma_commit_pair_w(&st->empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          if (kc == CHUNK_KB - 1 || kb == num_kb - 1) {
+            umma_commit_pair_w(&st->tmem_full[acc], 0x3);
+            if (++acc == ACC_BUFS) {
+              acc = 0;
+              acc_phase ^= 1u;
+            }
+          }
+        }
+      }
+      if (!ok && issued) {
+        umma_commit_pair_w(&st->drain, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs): chunk sums -> fp32 rows ----------------
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = (period % 4) == 0 && (row_stride % 4) == 0 && (batch_stride % 4) == 0 &&
+                        (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
+    const int chunks = (num_kb + CHUNK_KB - 1) / CHUNK_KB;
+    bool ok = true;
+    for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      int mb, nb;
+      tile_coords(t, tiles_m, tiles_n, mb, nb);
+      float sum[BN];
+#pragma unroll
+      for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+      for (int ch = 0; ch < chunks; ++ch) {
+        if (!warp_wait_gemm(&st->tmem_full[acc], acc_phase, abort_flag, err_word)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tbase =
+            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c0, r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[c0 + j] = __fadd_rn(sum[c0 + j], __uint_as_float(r[j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&st->tmem_empty[acc]), 0));
+        if (++acc == ACC_BUFS) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      const int row = mb * 2 * BM + static_cast<int>(rank) * BM + row_in_tile;
+      if (row < M) {
+        const float bias = row_bias ? __ldg(row_bias + row) : 0.0f;
+        if (row_bias || relu) {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) {
+            float v = sum[j] + bias;
+            sum[j] = relu ? fmaxf(v, 0.0f) : v;
+          }
+        }
+        const int col0 = nb * BN;
+        const int img = col0 / period, pix = col0 - img * period;
+        float* dst = C + static_cast<long long>(img) * batch_stride + static_cast<long long>(row) * row_stride + pix;
+        if (vec_ok && col0 + BN <= N && pix + BN <= period) {
+#pragma unroll
+          for (int q = 0; q < BN / 4; ++q)
+            reinterpret_cast<float4*>(dst)[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN; ++j) {
+            const int col = col0 + j;
+            if (col < N) {
+              const int im = col / period;
+              C[static_cast<long long>(im) * batch_stride + static_cast<long long>(row) * row_stride +
+                (col - im * period)] = sum[j];
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // neither CTA leaves while the pair's MMAs, commits or arrivals can touch it
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -478,7 +731,7 @@ size_t smem_bytes_for(int bn) { return 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * 
 // The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each), with bn-column tiles
 // (128, or 64 when 128-wide tiles would leave SMs idle: 1024^3 has 64 tiles of 128x128 for 148 SMs).
 cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                          int m, int n, int kp, const Epi& epi, cudaStream_t s, int bn = 128) {
+                          int m, int n, int kp, const Epi& epi, cudaStream_t s, int bn = 128, bool pair = false) {
   CUtensorMap mah, mal, mbh, mbl;
   if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
       !make_tmap_f32_2d(&mbh, b_hi, n, kp, bn, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, bn, BK))
@@ -492,6 +745,32 @@ cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, 
                                static_cast<int>(smem_bytes_for(64)));
     if (e != cudaSuccess) return e;
     attr_set = true;
+  }
+  if (pair) {
+    static bool pair_attr = false;  // benign race: idempotent attribute set
+    if (!pair_attr) {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(pairg::smem_bytes(128)));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(pairg::smem_bytes(64)));
+      if (e != cudaSuccess) return e;
+      pair_attr = true;
+    }
+    CUtensorMap pbh, pbl;  // B^T boxes of bn/2 rows: each CTA stages half of the tile's columns
+    if (!make_tmap_f32_2d(&pbh, b_hi, n, kp, bn / 2, BK) || !make_tmap_f32_2d(&pbl, b_lo, n, kp, bn / 2, BK))
+      return cudaErrorInvalidValue;
+    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + bn - 1) / bn);
+    const int clusters = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;
+    if (bn == 64)
+      gemm_tf32x3_pair_kernel<64><<<2 * clusters, pairg::NUM_THREADS, pairg::smem_bytes(64), s>>>(
+          mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+          ctx->err_word);
+    else
+      gemm_tf32x3_pair_kernel<128><<<2 * clusters, pairg::NUM_THREADS, pairg::smem_bytes(128), s>>>(
+          mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+          ctx->err_word);
+    return cudaGetLastError();
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
@@ -525,8 +804,15 @@ cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int
   if ((e = split(a, a_hi, a_lo, na, s)) == cudaSuccess) {
     tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
     if ((e = cudaGetLastError()) == cudaSuccess)
-      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s,
-                        static_cast<long long>((m + BM - 1) / BM) * ((n + 127) / 128) < ctx->sm_count ? 64 : 128);
+    {
+      // CTA pairs with 256x128 tiles, or 256x64 when the 128-wide tiles leave SM pairs idle (measured:
+      // 2048^3 0.112 -> 0.097 ms and 4096x1024x4096 0.181 -> 0.156 ms against one-CTA 128x128 tiles;
+      // 1024^3 0.034 ms with 256x64 pair tiles).
+      const long long pair_tiles = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * ((n + 127) / 128);
+      const int bn = pair_tiles < ctx->sm_count / 2 ? 64 : 128;
+      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s, bn,
+                        ctx->sm_count >= 2);
+    }
   }
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
