@@ -185,3 +185,22 @@ def test_reference_c_example_links_against_this_library():
         pytest.skip("oracle/_ref/c_api_example not built (needs the reference sources)")
     out = os.popen(f"ldd {exe}").read()
     assert "liblc_b200.so" in out and "not found" not in out, out
+
+
+def test_conv_sizes_beyond_int_rejected_before_gpu(lc):
+    """The conv launchers work in int: a reduction length in_channels*kh*kw, a padded extent or any
+    size argument beyond INT_MAX is LC_NOT_SUPPORTED before anything touches the GPU, in every conv
+    entry point (lcConv2dNchw, lcConvAttentionNchw, lcConvAttentionNchwNoAlloc, lcConvAutotune)."""
+    L = lc.lib
+    x = np.zeros(16, np.float32).ctypes.data_as(C.c_void_p)
+    big_c = 1 << 30  # 2^30 channels x 3 x 3 > INT_MAX
+    assert L.lcConv2dNchw(x, x, None, x, 1, big_c, 4, 4, 4, 3, 3, 1, 1, 1, 1, 0, None, None) == lc.LC_NOT_SUPPORTED
+    assert L.lcConvAttentionNchw(x, x, None, None, x, 1, big_c, 4, 4, 4, 3, 3, 1, 1, 1, 1, 4, 4, 0, 1, None,
+                                 None) == lc.LC_NOT_SUPPORTED
+    assert L.lcConvAttentionNchwNoAlloc(x, x, None, None, x, 1, big_c, 4, 4, 4, 3, 3, 1, 1, 1, 1, 4, 4, 0, 1,
+                                        None) == lc.LC_NOT_SUPPORTED
+    huge_pad = 1 << 31
+    assert L.lcConv2dNchw(x, x, None, x, 1, 4, 4, 4, 4, 3, 3, 1, 1, huge_pad, 1, 0, None, None) == lc.LC_NOT_SUPPORTED
+    buf = C.create_string_buffer(64)
+    assert L.lcConvAutotune(x, x, None, x, 1, big_c, 4, 4, 4, 3, 3, 1, 1, 1, 1, 0, None, buf, 64) == \
+        lc.LC_NOT_SUPPORTED
