@@ -19,6 +19,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <string>
 
 #include <mutex>
@@ -58,27 +59,6 @@ __device__ __forceinline__ float tf32_round(float x) {
   uint32_t u = __float_as_uint(x);
   if ((u & 0x7f800000u) != 0x7f800000u) u = (u + 0x1000u) & 0xffffe000u;
   return __uint_as_float(u);
-}
-
-// B [K,N] -> hi/lo planes of B^T [N,K]: 32x32 tiles through shared memory (coalesced both ways).
-__global__ void tf32_split_transpose_kernel(const float* __restrict__ b, float* __restrict__ hi_t,
-                                            float* __restrict__ lo_t, int K, int N) {
-  __shared__ float tile[32][33];
-  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int k = k0 + r, n = n0 + threadIdx.x;
-    tile[r][threadIdx.x] = (k < K && n < N) ? b[static_cast<size_t>(k) * N + n] : 0.0f;
-  }
-  __syncthreads();
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int n = n0 + r, k = k0 + threadIdx.x;
-    if (n < N && k < K) {
-      const float v = tile[threadIdx.x][r];
-      const float h = tf32_round(v);
-      hi_t[static_cast<size_t>(n) * K + k] = h;
-      lo_t[static_cast<size_t>(n) * K + k] = v - h;
-    }
-  }
 }
 
 // Rows of src [rows, k] -> hi/lo planes [rows, kp] (kp >= k, zero padded).
@@ -154,22 +134,47 @@ __global__ void __launch_bounds__(256) tf32_im2col_split_kernel(const float* __r
   }
 }
 
-// hi = tf32(x), lo = x - hi, four elements per thread.
-__global__ void tf32_split_kernel(const float4* __restrict__ x, float4* __restrict__ hi, float4* __restrict__ lo,
-                                  size_t n4) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
-    const float4 v = x[i];
-    float4 h, l;
-    h.x = tf32_round(v.x);
-    h.y = tf32_round(v.y);
-    h.z = tf32_round(v.z);
-    h.w = tf32_round(v.w);
-    l.x = v.x - h.x;
-    l.y = v.y - h.y;
-    l.z = v.z - h.z;
-    l.w = v.w - h.w;
-    hi[i] = h;
-    lo[i] = l;
+// The matmul's pre-pass in one launch: blocks [0, a_blocks) split A [M,K] into hi/lo planes
+// (grid-stride over float4s), the rest split B [K,N] into the hi/lo planes of B^T [N,K] by 32x32
+// tiles through shared memory; block 0 also zeroes the split-K counters of the GEMM that follows.
+__global__ void __launch_bounds__(256) tf32_matmul_prep_kernel(const float4* __restrict__ a, float4* __restrict__ a_hi,
+                                                               float4* __restrict__ a_lo, size_t na4, int a_blocks,
+                                                               const float* __restrict__ b, float* __restrict__ bh_t,
+                                                               float* __restrict__ bl_t, int K, int N, int bt_x,
+                                                               unsigned* __restrict__ counters, int n_counters) {
+  __shared__ float tile[32][33];
+  const int bid = static_cast<int>(blockIdx.x);
+  if (bid == 0)
+    for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0u;
+  if (bid < a_blocks) {
+    for (size_t i = static_cast<size_t>(bid) * 256 + threadIdx.x; i < na4; i += static_cast<size_t>(a_blocks) * 256) {
+      const float4 v = a[i];
+      float4 h;
+      h.x = tf32_round(v.x);
+      h.y = tf32_round(v.y);
+      h.z = tf32_round(v.z);
+      h.w = tf32_round(v.w);
+      a_hi[i] = h;
+      a_lo[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+    }
+    return;
+  }
+  const int bt = bid - a_blocks;
+  const int k0 = (bt / bt_x) * 32, n0 = (bt % bt_x) * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < 32; r += 8) {
+    const int k = k0 + r, n = n0 + tx;
+    tile[r][tx] = (k < K && n < N) ? b[static_cast<size_t>(k) * N + n] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int n = n0 + r, k = k0 + tx;
+    if (n < N && k < K) {
+      const float v = tile[tx][r];
+      const float h = tf32_round(v);
+      bh_t[static_cast<size_t>(n) * K + k] = h;
+      bl_t[static_cast<size_t>(n) * K + k] = v - h;
+    }
   }
 }
 
@@ -432,36 +437,60 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- cluster-pair variant ---------------------------------------------------------------------
 // Two CTAs (two SMs) compute a 256 x BN tile with tcgen05.mma.cta_group::2.kind::tf32 (M = 256,
-// N = BN, K = 8): each CTA stages its own 128 rows of the A planes and half of the B^T rows, so a
-// stage is 32 KB + BN x 128 B and four stages fit; the leader issues every MMA, its commits release
-// the stage in both CTAs and hand each CTA its accumulator lanes chunk by chunk; each CTA's
-// epilogue folds its rows' chunks into fp32 registers exactly as the one-CTA kernel does.
+// N = BN, K = 8): each CTA stages its own 128 rows of the A planes and half of the B^T rows; the
+// leader issues every MMA, its commits release the stage in both CTAs and hand each CTA its
+// accumulator lanes chunk by chunk; each CTA's epilogue folds its rows' chunks into fp32 registers
+// exactly as the one-CTA kernel does.
+//
+// Split K: a work item is (tile, split) with `kb_per` k-blocks per split.  With ksplit > 1 every
+// epilogue warp writes its 32 rows x COLS partial sums (column-major, so a warp's store is one
+// 128-byte line per column) and bumps its own counter; the warp that brings the counter to ksplit
+// adds all partials in split order (0, 1, ..., its own registers at its own position), so the
+// result does not depend on which split finishes last.  The counters are zeroed by the plane
+// pre-pass of the same call.
 namespace pairg {
-constexpr int STAGES = 4;
-constexpr int NUM_THREADS = 192;
+template <int BN>
+struct Cfg {
+  static_assert(BN == 64 || BN == 128, "pair tile width");
+  static constexpr int EPI_WARPS = 4;              // one per TMEM lane quarter
+  static constexpr int COLS = BN * 4 / EPI_WARPS;  // columns per epilogue warp (the whole tile row)
+  static constexpr int STAGES = 4;
+  static constexpr int ACC = 4;                    // TMEM chunk buffers of BN columns
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * (BN / 2) * BK * 4;
+};
 struct Tail {
-  uint64_t full[STAGES];          // leader: both CTAs' bytes of the stage landed
-  uint64_t empty[STAGES];         // per CTA: the leader's MMAs reading this stage finished
-  uint64_t tmem_full[ACC_BUFS];   // per CTA: its lanes of a K chunk's partial sum are in buffer b
-  uint64_t tmem_empty[ACC_BUFS];  // leader: the 8 epilogue warps of both CTAs folded buffer b
+  uint64_t full[4];          // leader: both CTAs' bytes of the stage landed
+  uint64_t empty[4];         // per CTA: the leader's MMAs reading this stage finished
+  uint64_t tmem_full[4];     // per CTA: its lanes of a K chunk's partial sum are in buffer b
+  uint64_t tmem_empty[4];    // leader: the epilogue warps of both CTAs folded buffer b
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t smem_bytes(int bn) { return 1024 + STAGES * (2 * A_PLANE_BYTES + bn * BK * 4) + sizeof(Tail); }
+template <int BN>
+constexpr size_t smem_bytes() {
+  return 1024 + Cfg<BN>::STAGES * Cfg<BN>::STAGE_BYTES + sizeof(Tail);
+}
 }  // namespace pairg
 
 template <int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::Cfg<BN>::THREADS, 1)
     gemm_tf32x3_pair_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                             const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                             float* __restrict__ C, int M, int N, int K, int period, long long batch_stride,
-                            long long row_stride, const float* __restrict__ row_bias, int relu, unsigned* err_word) {
+                            long long row_stride, const float* __restrict__ row_bias, int relu, int ksplit,
+                            int kb_per, float* __restrict__ part, unsigned* __restrict__ counters,
+                            unsigned* err_word) {
   using pairg::Tail;
-  constexpr int STAGES = pairg::STAGES;
+  using CF = pairg::Cfg<BN>;
+  constexpr int STAGES = CF::STAGES;
+  constexpr int ACC = CF::ACC;
+  constexpr int COLS = CF::COLS;
   constexpr int B_HALF_PLANE = (BN / 2) * BK * 4;
-  constexpr int STAGE_BYTES = 2 * A_PLANE_BYTES + 2 * B_HALF_PLANE;  // A_hi | A_lo | B_hi | B_lo (this CTA's half)
+  constexpr int STAGE_BYTES = CF::STAGE_BYTES;  // A_hi | A_lo | B_hi | B_lo (this CTA's half)
   constexpr uint32_t IDESC = idesc_tf32_f32(2 * BM, BN, 0, 0);
+  static_assert(ACC * BN <= TMEM_COLS, "TMEM chunk buffers");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Tail* st = reinterpret_cast<Tail*>(smem + STAGES * STAGE_BYTES);
@@ -475,15 +504,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
   const int tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + BK - 1) / BK;
+  const int num_items = num_tiles * ksplit;
+  auto item_range = [&](int w, int& t, int& sp, int& kb0, int& kb1) {
+    t = w / ksplit;
+    sp = w - t * ksplit;
+    kb0 = sp * kb_per;
+    kb1 = min(num_kb, kb0 + kb_per);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&st->full[s], 1);
       mbar_init(&st->empty[s], 1);
     }
-    for (int b = 0; b < ACC_BUFS; ++b) {
+    for (int b = 0; b < ACC; ++b) {
       mbar_init(&st->tmem_full[b], 1);
-      mbar_init(&st->tmem_empty[b], 8);
+      mbar_init(&st->tmem_empty[b], 2 * CF::EPI_WARPS);
     }
     mbar_init(&st->drain, 1);
     st->abort_flag = 0;
@@ -510,12 +546,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-        int mb, nb;
+      for (int w = cluster_id; w < num_items && ok; w += num_clusters) {
+        int t, sp, kb0, kb1, mb, nb;
+        item_range(w, t, sp, kb0, kb1);
         tile_coords(t, tiles_m, tiles_n, mb, nb);
         const int row0 = mb * 2 * BM + static_cast<int>(rank) * BM;
         const int col0 = nb * BN + static_cast<int>(rank) * (BN / 2);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&st->empty[stage], phase ^ 1u, abort_flag, err_word, kErrGemmProducerWait)) {
             ok = false;
             break;
@@ -550,10 +587,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, issued = false;
-      for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
+      for (int w = cluster_id; w < num_items && ok; w += num_clusters) {
+        int t, sp, kb0, kb1;
+        item_range(w, t, sp, kb0, kb1);
         uint32_t d_tmem = tmem_base;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          const int kc = kb % CHUNK_KB;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          const int kc = (kb - kb0) % CHUNK_KB;
           if (kc == 0) {
             if (!warp_wait_poll(&st->tmem_empty[acc], acc_phase ^ 1u, abort_flag, err_word, kErrGemmMmaWait)) {
               ok = false;
@@ -585,9 +624,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
             stage = 0;
             phase ^= 1u;
           }
-          if (kc == CHUNK_KB - 1 || kb == num_kb - 1) {
+          if (kc == CHUNK_KB - 1 || kb == kb1 - 1) {
             umma_commit_pair_w(&st->tmem_full[acc], 0x3);
-            if (++acc == ACC_BUFS) {
+            if (++acc == ACC) {
               acc = 0;
               acc_phase ^= 1u;
             }
@@ -602,31 +641,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
       }
     }
   } else {
-    // ---------------- epilogue (warps 2..5 of both CTAs): chunk sums -> fp32 rows ----------------
-    const int quarter = warp & 3;
+    // ---------------- epilogue (warps 2.. of both CTAs): chunk sums -> fp32 rows ----------------
+    const int quarter = warp & 3;                  // TMEM lane quarter this warp may read
+    const int ew = warp - 2;                       // epilogue warp index
+    const int cbase = (ew >> 2) * COLS;            // this warp's first column of the tile
     const int row_in_tile = quarter * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec_ok = (period % 4) == 0 && (row_stride % 4) == 0 && (batch_stride % 4) == 0 &&
                         (reinterpret_cast<uintptr_t>(C) & 15u) == 0;
-    const int chunks = (num_kb + CHUNK_KB - 1) / CHUNK_KB;
     bool ok = true;
-    for (int t = cluster_id; t < num_tiles && ok; t += num_clusters) {
-      int mb, nb;
+    for (int w = cluster_id; w < num_items && ok; w += num_clusters) {
+      int t, sp, kb0, kb1, mb, nb;
+      item_range(w, t, sp, kb0, kb1);
       tile_coords(t, tiles_m, tiles_n, mb, nb);
-      float sum[BN];
+      const int chunks = (kb1 - kb0 + CHUNK_KB - 1) / CHUNK_KB;
+      float sum[COLS];
 #pragma unroll
-      for (int j = 0; j < BN; ++j) sum[j] = 0.0f;
+      for (int j = 0; j < COLS; ++j) sum[j] = 0.0f;
       for (int ch = 0; ch < chunks; ++ch) {
         if (!warp_wait_gemm(&st->tmem_full[acc], acc_phase, abort_flag, err_word)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tbase =
-            tmem_base + static_cast<uint32_t>(acc * BN) + (static_cast<uint32_t>(quarter * 32) << 16);
+        const uint32_t tbase = tmem_base + static_cast<uint32_t>(acc * BN + cbase) +
+                               (static_cast<uint32_t>(quarter * 32) << 16);
 #pragma unroll
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        for (int c0 = 0; c0 < COLS; c0 += 32) {
           uint32_t r[32];
           tmem_ld32(tbase + c0, r);
 #pragma unroll
@@ -635,32 +677,87 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::NUM_THREADS, 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&st->tmem_empty[acc]), 0));
-        if (++acc == ACC_BUFS) {
+        if (++acc == ACC) {
           acc = 0;
           acc_phase ^= 1u;
         }
       }
       if (!ok) break;
+      if (ksplit > 1) {
+        // This warp's partial block: [tile][split][rank][epilogue warp][COLS][32 lanes].
+        const long long wblk = (static_cast<long long>(t) * 2 + rank) * CF::EPI_WARPS + ew;
+        const long long span = static_cast<long long>(num_tiles) * 2 * CF::EPI_WARPS * COLS * 32;
+        float* mine = part + sp * span + wblk * COLS * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < COLS; ++j) __stcg(mine + j * 32, sum[j]);
+        __threadfence();
+        __syncwarp();
+        unsigned prev = 0;
+        if (lane == 0) prev = atomicAdd(counters + wblk, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev != static_cast<unsigned>(ksplit - 1)) continue;  // another split finishes this block
+        __threadfence();
+        // Last split of this block: every split's partial (its own included) from L2, added in
+        // split order, 32 columns at a time, then bias/ReLU and the store.
+        const int row = mb * 2 * BM + static_cast<int>(rank) * BM + row_in_tile;
+        const float* first = part + wblk * COLS * 32 + lane;
+        const float bias = (row_bias && row < M) ? __ldg(row_bias + row) : 0.0f;
+#pragma unroll 1
+        for (int jc = 0; jc < COLS; jc += 32) {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __ldcg(first + (jc + i) * 32);
+          for (int q = 1; q < ksplit; ++q) {
+            const float* pq = first + q * span + jc * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], __ldcg(pq + i * 32));
+          }
+          if (row >= M) continue;
+          if (row_bias || relu) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = relu ? fmaxf(v[i] + bias, 0.0f) : v[i] + bias;
+          }
+          const int col0 = nb * BN + cbase + jc;
+          const int img = col0 / period, pix = col0 - img * period;
+          float* dst = C + static_cast<long long>(img) * batch_stride + static_cast<long long>(row) * row_stride + pix;
+          if (vec_ok && col0 + 32 <= N && pix + 32 <= period) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = col0 + i;
+              if (col < N) {
+                const int im = col / period;
+                C[static_cast<long long>(im) * batch_stride + static_cast<long long>(row) * row_stride +
+                  (col - im * period)] = v[i];
+              }
+            }
+          }
+        }
+        continue;
+      }
       const int row = mb * 2 * BM + static_cast<int>(rank) * BM + row_in_tile;
       if (row < M) {
         const float bias = row_bias ? __ldg(row_bias + row) : 0.0f;
         if (row_bias || relu) {
 #pragma unroll
-          for (int j = 0; j < BN; ++j) {
+          for (int j = 0; j < COLS; ++j) {
             float v = sum[j] + bias;
             sum[j] = relu ? fmaxf(v, 0.0f) : v;
           }
         }
-        const int col0 = nb * BN;
+        const int col0 = nb * BN + cbase;
         const int img = col0 / period, pix = col0 - img * period;
         float* dst = C + static_cast<long long>(img) * batch_stride + static_cast<long long>(row) * row_stride + pix;
-        if (vec_ok && col0 + BN <= N && pix + BN <= period) {
+        if (vec_ok && col0 + COLS <= N && pix + COLS <= period) {
 #pragma unroll
-          for (int q = 0; q < BN / 4; ++q)
+          for (int q = 0; q < COLS / 4; ++q)
             reinterpret_cast<float4*>(dst)[q] = make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN; ++j) {
+          for (int j = 0; j < COLS; ++j) {
             const int col = col0 + j;
             if (col < N) {
               const int im = col / period;
@@ -700,14 +797,6 @@ bool make_tmap_f32_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-cudaError_t split(const float* x, float* hi, float* lo, size_t n, cudaStream_t s) {
-  const size_t n4 = n / 4;  // callers keep n a multiple of 4
-  const int blocks = static_cast<int>(n4 / 256 + 1 < 148 * 8 ? n4 / 256 + 1 : 148 * 8);
-  tf32_split_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const float4*>(x), reinterpret_cast<float4*>(hi),
-                                            reinterpret_cast<float4*>(lo), n4);
-  return cudaGetLastError();
-}
-
 }  // namespace
 
 bool gemm_f32_tc_supported(const void* a, const void* b, const void* c, int m, int k, int n) {
@@ -730,8 +819,10 @@ size_t smem_bytes_for(int bn) { return 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * 
 
 // The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each), with bn-column tiles
 // (128, or 64 when 128-wide tiles would leave SMs idle: 1024^3 has 64 tiles of 128x128 for 148 SMs).
+// The GEMM on prepared planes A [m, kp] and B^T [n, kp] (hi and lo of each) with the one-CTA
+// kernel, bn-column tiles (128, or 64 when 128-wide tiles would leave SMs idle).
 cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
-                          int m, int n, int kp, const Epi& epi, cudaStream_t s, int bn = 128, bool pair = false) {
+                          int m, int n, int kp, const Epi& epi, cudaStream_t s, int bn = 128) {
   CUtensorMap mah, mal, mbh, mbl;
   if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
       !make_tmap_f32_2d(&mbh, b_hi, n, kp, bn, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, bn, BK))
@@ -746,32 +837,6 @@ cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, 
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
-  if (pair) {
-    static bool pair_attr = false;  // benign race: idempotent attribute set
-    if (!pair_attr) {
-      cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(pairg::smem_bytes(128)));
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 static_cast<int>(pairg::smem_bytes(64)));
-      if (e != cudaSuccess) return e;
-      pair_attr = true;
-    }
-    CUtensorMap pbh, pbl;  // B^T boxes of bn/2 rows: each CTA stages half of the tile's columns
-    if (!make_tmap_f32_2d(&pbh, b_hi, n, kp, bn / 2, BK) || !make_tmap_f32_2d(&pbl, b_lo, n, kp, bn / 2, BK))
-      return cudaErrorInvalidValue;
-    const int tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + bn - 1) / bn);
-    const int clusters = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;
-    if (bn == 64)
-      gemm_tf32x3_pair_kernel<64><<<2 * clusters, pairg::NUM_THREADS, pairg::smem_bytes(64), s>>>(
-          mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
-          ctx->err_word);
-    else
-      gemm_tf32x3_pair_kernel<128><<<2 * clusters, pairg::NUM_THREADS, pairg::smem_bytes(128), s>>>(
-          mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
-          ctx->err_word);
-    return cudaGetLastError();
-  }
   const int tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
   if (bn == 64)
@@ -785,6 +850,66 @@ cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, 
   return cudaGetLastError();
 }
 
+// Work plan of the cluster-pair matmul: tile width, K splits and k-blocks per split.
+struct PairPlan {
+  int bn, ksplit, kb_per, tiles;
+  size_t part_floats, counters;
+};
+
+PairPlan plan_pair(const DeviceCtx* ctx, int m, int n, int k, int bn) {
+  PairPlan pl{};
+  pl.bn = bn;
+  const int clusters = ctx->sm_count / 2;
+  const int num_kb = (k + BK - 1) / BK;
+  pl.tiles = ((m + 2 * BM - 1) / (2 * BM)) * ((n + bn - 1) / bn);
+  int ks = 1;
+  // Fewer tiles than half the SM pairs: split K so the pairs fill up, keeping at least one
+  // 128-deep chunk per split.
+  if (pl.tiles * 2 <= clusters) ks = std::max(1, std::min(clusters / pl.tiles, num_kb / CHUNK_KB));
+  pl.kb_per = (num_kb + ks - 1) / ks;
+  pl.ksplit = (num_kb + pl.kb_per - 1) / pl.kb_per;  // every split non-empty
+  const int epi_warps = pairg::Cfg<128>::EPI_WARPS;
+  pl.part_floats = pl.ksplit > 1 ? static_cast<size_t>(pl.ksplit) * pl.tiles * 2 * BM * bn : 0;
+  pl.counters = static_cast<size_t>(pl.tiles) * 2 * epi_warps;
+  return pl;
+}
+
+template <int BN>
+cudaError_t launch_pair_bn(const CUtensorMap& mah, const CUtensorMap& mal, const CUtensorMap& pbh,
+                           const CUtensorMap& pbl, int m, int n, int kp, const Epi& epi, const PairPlan& pl,
+                           float* part, unsigned* counters, unsigned* err_word, int clusters_max, cudaStream_t s) {
+  static bool attr = false;  // benign race: idempotent attribute set
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(pairg::smem_bytes<BN>()));
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int items = pl.tiles * pl.ksplit;
+  const int clusters = items < clusters_max ? items : clusters_max;
+  gemm_tf32x3_pair_kernel<BN><<<2 * clusters, pairg::Cfg<BN>::THREADS, pairg::smem_bytes<BN>(), s>>>(
+      mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
+      pl.ksplit, pl.kb_per, part, counters, err_word);
+  return cudaGetLastError();
+}
+
+// The matmul on prepared planes with CTA pairs (256-row tiles), per `pl`.
+cudaError_t launch_pair(DeviceCtx* ctx, const float* a_hi, const float* a_lo, const float* b_hi, const float* b_lo,
+                        int m, int n, int kp, const Epi& epi, const PairPlan& pl, float* part, unsigned* counters,
+                        cudaStream_t s) {
+  CUtensorMap mah, mal, pbh, pbl;  // B^T boxes of bn/2 rows: each CTA stages half of the tile's columns
+  if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
+      !make_tmap_f32_2d(&pbh, b_hi, n, kp, pl.bn / 2, BK) || !make_tmap_f32_2d(&pbl, b_lo, n, kp, pl.bn / 2, BK))
+    return cudaErrorInvalidValue;
+  const int cmax = ctx->sm_count / 2;
+  switch (pl.bn) {
+    case 64:
+      return launch_pair_bn<64>(mah, mal, pbh, pbl, m, n, kp, epi, pl, part, counters, ctx->err_word, cmax, s);
+    default:
+      return launch_pair_bn<128>(mah, mal, pbh, pbl, m, n, kp, epi, pl, part, counters, ctx->err_word, cmax, s);
+  }
+}
+
 int grid_for(long long n) { return static_cast<int>(n / 256 + 1 < 148 * 8 ? n / 256 + 1 : 148 * 8); }
 
 }  // namespace
@@ -792,28 +917,34 @@ int grid_for(long long n) { return static_cast<int>(n / 256 + 1 < 148 * 8 ? n / 
 cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int k, int n, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
+  if (ctx->sm_count < 2) return cudaErrorNotSupported;
   const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
-  // Split planes in a stream-ordered workspace: allocated and freed on `s` around the kernels.
+  // CTA pairs with 256x128 tiles, or 256x64 when the wider tiles would leave SM pairs idle; K is
+  // split across pairs only when even the 256x64 tiles fill fewer than half of them (measured:
+  // 1024^3 0.034 -> 0.030 ms with the one-launch pre-pass; [512, 4096, 512] 0.037 ms with 4 splits;
+  // 256x256 tiles were slower at every size tried).
+  const long long wide_tiles = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * ((n + 127) / 128);
+  const int bn = wide_tiles < ctx->sm_count / 2 ? 64 : 128;
+  const PairPlan pl = plan_pair(ctx, m, n, k, bn);
+  // Stream-ordered workspace: the split planes, the split-K partial sums and the counters.
+  const size_t planes = 2 * (na + nb);
   float* ws = nullptr;
-  cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws), 2 * (na + nb) * sizeof(float), s);
+  cudaError_t e = workspace_alloc(ctx, reinterpret_cast<void**>(&ws),
+                                  (planes + pl.part_floats + pl.counters) * sizeof(float), s);
   if (e != cudaSuccess) return e;
   float* a_hi = ws;
   float* a_lo = a_hi + na;
   float* b_hi = a_lo + na;
   float* b_lo = b_hi + nb;
-  if ((e = split(a, a_hi, a_lo, na, s)) == cudaSuccess) {
-    tf32_split_transpose_kernel<<<dim3((n + 31) / 32, (k + 31) / 32), dim3(32, 8), 0, s>>>(b, b_hi, b_lo, k, n);
-    if ((e = cudaGetLastError()) == cudaSuccess)
-    {
-      // CTA pairs with 256x128 tiles, or 256x64 when the 128-wide tiles leave SM pairs idle (measured:
-      // 2048^3 0.112 -> 0.097 ms and 4096x1024x4096 0.181 -> 0.156 ms against one-CTA 128x128 tiles;
-      // 1024^3 0.034 ms with 256x64 pair tiles).
-      const long long pair_tiles = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * ((n + 127) / 128);
-      const int bn = pair_tiles < ctx->sm_count / 2 ? 64 : 128;
-      e = launch_planes(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, s, bn,
-                        ctx->sm_count >= 2);
-    }
-  }
+  float* part = ws + planes;
+  unsigned* counters = reinterpret_cast<unsigned*>(part + pl.part_floats);
+  const int a_blocks = static_cast<int>(std::min<size_t>((na / 4 + 255) / 256, 1184));
+  const int bt_x = (n + 31) / 32, bt_y = (k + 31) / 32;
+  tf32_matmul_prep_kernel<<<a_blocks + bt_x * bt_y, 256, 0, s>>>(
+      reinterpret_cast<const float4*>(a), reinterpret_cast<float4*>(a_hi), reinterpret_cast<float4*>(a_lo), na / 4,
+      a_blocks, b, b_hi, b_lo, k, n, bt_x, counters, static_cast<int>(pl.counters));
+  if ((e = cudaGetLastError()) == cudaSuccess)
+    e = launch_pair(ctx, a_hi, a_lo, b_hi, b_lo, m, n, k, Epi{c, n, 0, n, nullptr, 0}, pl, part, counters, s);
   const cudaError_t ef = workspace_free(ws, s);
   return e != cudaSuccess ? e : ef;
 }

@@ -117,3 +117,22 @@ def test_conv_attention_config5_all_images(gpu):
     pick = [0, 15, 31]
     ref = P.conv_attention_images(np.ascontiguousarray(x[pick]), w, bias, pw, 3136, 64, threads=3)
     close_enough(ref, got[pick], *F32_TOL)
+
+
+@pytest.mark.parametrize("m,k,n", [(512, 4096, 512), (512, 1188, 520), (300, 2052, 260)])
+def test_matmul_f32_split_k(gpu, m, k, n):
+    """Shapes whose 256x64 pair tiles fill under half of the SM pairs, so K is split across pairs
+    (uneven last split, ragged M and N edges): the split partial sums are added by whichever split
+    finishes last, in split order.  Every row against the oracle at 1e-4 + 1e-4|ref|."""
+    import torch
+
+    g = torch.Generator(device="cuda").manual_seed(11)
+    a = torch.rand((m, k), generator=g, device="cuda") * 2 - 1
+    b = torch.rand((k, n), generator=g, device="cuda") * 2 - 1
+    c = torch.full((m, n), float("nan"), device="cuda")
+    outs = []
+    for _ in range(2):  # the same bits on a repeat: the split order fixes the summation order
+        _run(gpu, torch, a, b, c, m, k, n, gpu.F32)
+        outs.append(c.cpu().numpy().copy())
+    assert np.array_equal(outs[0], outs[1])
+    close_enough(P.matmul(a.cpu().numpy(), b.cpu().numpy(), threads=8), outs[0], *F32_TOL)
