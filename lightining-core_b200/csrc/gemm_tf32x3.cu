@@ -443,11 +443,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // exactly as the one-CTA kernel does.
 //
 // Split K: a work item is (tile, split) with `kb_per` k-blocks per split.  With ksplit > 1 every
-// epilogue warp writes its 32 rows x COLS partial sums (column-major, so a warp's store is one
-// 128-byte line per column) and bumps its own counter; the warp that brings the counter to ksplit
-// adds all partials in split order (0, 1, ..., its own registers at its own position), so the
-// result does not depend on which split finishes last.  The counters are zeroed by the plane
-// pre-pass of the same call.
+// epilogue warp writes its 32 rows x COLS partial sums to an L2 workspace and bumps its own
+// counter; the warp that brings the counter to ksplit adds the partials (two splits: its own
+// registers plus the other one, which is order-free; more: all of them in split order), so the
+// bits never depend on which split finished last.  The counters are zeroed by the pre-pass of the
+// same call.
 namespace pairg {
 template <int BN>
 struct Cfg {
@@ -684,12 +684,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::Cfg<BN>::THRE
       }
       if (!ok) break;
       if (ksplit > 1) {
-        // This warp's partial block: [tile][split][rank][epilogue warp][COLS][32 lanes].
+        // This warp's partial block: [tile][split][rank][epilogue warp] of COLS/4 x 32 float4s
+        // (quad q of lane l at q * 32 + l: every store and load of the warp is 512 contiguous bytes).
         const long long wblk = (static_cast<long long>(t) * 2 + rank) * CF::EPI_WARPS + ew;
-        const long long span = static_cast<long long>(num_tiles) * 2 * CF::EPI_WARPS * COLS * 32;
-        float* mine = part + sp * span + wblk * COLS * 32 + lane;
+        const long long span4 = static_cast<long long>(num_tiles) * 2 * CF::EPI_WARPS * (COLS / 4) * 32;
+        float4* blk = reinterpret_cast<float4*>(part) + wblk * (COLS / 4) * 32 + lane;
 #pragma unroll
-        for (int j = 0; j < COLS; ++j) __stcg(mine + j * 32, sum[j]);
+        for (int q = 0; q < COLS / 4; ++q)
+          __stcg(blk + sp * span4 + q * 32, make_float4(sum[4 * q], sum[4 * q + 1], sum[4 * q + 2], sum[4 * q + 3]));
         __threadfence();
         __syncwarp();
         unsigned prev = 0;
@@ -697,46 +699,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::Cfg<BN>::THRE
         prev = __shfl_sync(0xffffffffu, prev, 0);
         if (prev != static_cast<unsigned>(ksplit - 1)) continue;  // another split finishes this block
         __threadfence();
-        // Last split of this block: every split's partial (its own included) from L2, added in
-        // split order, 32 columns at a time, then bias/ReLU and the store.
-        const int row = mb * 2 * BM + static_cast<int>(rank) * BM + row_in_tile;
-        const float* first = part + wblk * COLS * 32 + lane;
-        const float bias = (row_bias && row < M) ? __ldg(row_bias + row) : 0.0f;
-#pragma unroll 1
-        for (int jc = 0; jc < COLS; jc += 32) {
-          float v[32];
+        // Last split of this block.  Two splits: own + other (a + b == b + a, so the bits do not
+        // depend on which split came last).  More: every partial from L2 in split order.  16
+        // float4 loads are in flight per lane at a time.
+        if (ksplit == 2) {
+          const float4* other = blk + (1 - sp) * span4;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __ldcg(first + (jc + i) * 32);
-          for (int q = 1; q < ksplit; ++q) {
-            const float* pq = first + q * span + jc * 32;
+          for (int h = 0; h < COLS / 64; ++h) {
+            float4 v[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], __ldcg(pq + i * 32));
+            for (int i = 0; i < 16; ++i) v[i] = __ldcg(other + (h * 16 + i) * 32);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float* sj = sum + (h * 16 + i) * 4;
+              sj[0] = __fadd_rn(sj[0], v[i].x);
+              sj[1] = __fadd_rn(sj[1], v[i].y);
+              sj[2] = __fadd_rn(sj[2], v[i].z);
+              sj[3] = __fadd_rn(sj[3], v[i].w);
+            }
           }
-          if (row >= M) continue;
-          if (row_bias || relu) {
+        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = relu ? fmaxf(v[i] + bias, 0.0f) : v[i] + bias;
-          }
-          const int col0 = nb * BN + cbase + jc;
-          const int img = col0 / period, pix = col0 - img * period;
-          float* dst = C + static_cast<long long>(img) * batch_stride + static_cast<long long>(row) * row_stride + pix;
-          if (vec_ok && col0 + 32 <= N && pix + 32 <= period) {
+          for (int h = 0; h < COLS / 64; ++h) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-          } else {
+            for (int i = 0; i < 16; ++i) {
+              const float4 v = __ldcg(blk + (h * 16 + i) * 32);
+              float* sj = sum + (h * 16 + i) * 4;
+              sj[0] = v.x, sj[1] = v.y, sj[2] = v.z, sj[3] = v.w;
+            }
+            for (int q = 1; q < ksplit; ++q) {
+              float4 v[16];
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const int col = col0 + i;
-              if (col < N) {
-                const int im = col / period;
-                C[static_cast<long long>(im) * batch_stride + static_cast<long long>(row) * row_stride +
-                  (col - im * period)] = v[i];
+              for (int i = 0; i < 16; ++i) v[i] = __ldcg(blk + q * span4 + (h * 16 + i) * 32);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float* sj = sum + (h * 16 + i) * 4;
+                sj[0] = __fadd_rn(sj[0], v[i].x);
+                sj[1] = __fadd_rn(sj[1], v[i].y);
+                sj[2] = __fadd_rn(sj[2], v[i].z);
+                sj[3] = __fadd_rn(sj[3], v[i].w);
               }
             }
           }
         }
-        continue;
       }
       const int row = mb * 2 * BM + static_cast<int>(rank) * BM + row_in_tile;
       if (row < M) {
@@ -919,12 +924,12 @@ cudaError_t gemm_f32_3xtf32(const float* a, const float* b, float* c, int m, int
   if (!ctx) return cudaErrorNoDevice;
   if (ctx->sm_count < 2) return cudaErrorNotSupported;
   const size_t na = static_cast<size_t>(m) * k, nb = static_cast<size_t>(k) * n;
-  // CTA pairs with 256x128 tiles, or 256x64 when the wider tiles would leave SM pairs idle; K is
-  // split across pairs only when even the 256x64 tiles fill fewer than half of them (measured:
-  // 1024^3 0.034 -> 0.030 ms with the one-launch pre-pass; [512, 4096, 512] 0.037 ms with 4 splits;
-  // 256x256 tiles were slower at every size tried).
+  // CTA pairs with 256x128 tiles; 256x64 when the wider tiles fill between a quarter and a half
+  // of the SM pairs; with fewer tiles K is split across pairs (plan_pair).  Measured: 1024^3
+  // 0.034 -> 0.029 ms (one-launch pre-pass, 256x128 tiles in two K splits), 2048^3 0.097 ms;
+  // 256x256 tiles (eight epilogue warps, three stages) were slower at every size tried.
   const long long wide_tiles = static_cast<long long>((m + 2 * BM - 1) / (2 * BM)) * ((n + 127) / 128);
-  const int bn = wide_tiles < ctx->sm_count / 2 ? 64 : 128;
+  const int bn = (wide_tiles < ctx->sm_count / 2 && wide_tiles * 4 > ctx->sm_count) ? 64 : 128;
   const PairPlan pl = plan_pair(ctx, m, n, k, bn);
   // Stream-ordered workspace: the split planes, the split-K partial sums and the counters.
   const size_t planes = 2 * (na + nb);
