@@ -604,6 +604,33 @@ def extra_configs(args, lc, torch, dev, sp):
     for key in [k for k in res if k.startswith(("cfg1", "cfg2", "cfg5"))]:
         res[key]["frac_fp32_simt_nominal"] = res[key]["tflops"] / 74.4
         res[key]["frac_3xtf32_nominal"] = res[key]["tflops"] / 375.0
+    # Config 4's GEMM sweep (bf16 in/out, fp32 accumulate), each size through lcMatMul's default
+    # dispatch, L2 flushed before every timed launch (CUDA events on the launching stream).
+    bf_peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for (m, k, n) in ((4096, 4096, 4096), (16384, 16384, 16384), (16384, 1024, 4096)):
+        g.manual_seed(3)
+        a = ((torch.rand((m, k), generator=g, device=dev) * 2 - 1) / k ** 0.5).to(torch.bfloat16)
+        b = ((torch.rand((k, n), generator=g, device=dev) * 2 - 1) / k ** 0.5).to(torch.bfloat16)
+        c = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+        run = lambda: lc.check(L.lcMatMul(ptr(a), ptr(b), ptr(c), m, k, n, lc.BF16, None, sp))  # noqa: E731
+        for _ in range(3):
+            run()
+        times = []
+        for _ in range(5):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            run()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        ms = sorted(times)[len(times) // 2]
+        tf = 2.0 * m * k * n / (ms * 1e-3) / 1e12
+        res[f"cfg4_matmul_bf16_{m}x{k}x{n}"] = {"ms": ms, "tflops": tf, "frac_of_bf16_peak": tf / bf_peak,
+                                                "timing": "median of 5, L2 flushed before each"}
+        del a, b, c
+    del flush
     rows, cols = 65536, 1024
     x = torch.randn((rows, cols), device=dev)
     y = torch.empty_like(x)
