@@ -608,7 +608,7 @@ def extra_configs(args, lc, torch, dev, sp):
     # dispatch, L2 flushed before every timed launch (CUDA events on the launching stream).
     bf_peak = float(pk.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    for (m, k, n) in ((4096, 4096, 4096), (16384, 16384, 16384), (16384, 1024, 4096)):
+    for (m, k, n) in ((16384, 1024, 4096), (4096, 4096, 4096), (16384, 16384, 16384)):
         g.manual_seed(3)
         a = ((torch.rand((m, k), generator=g, device=dev) * 2 - 1) / k ** 0.5).to(torch.bfloat16)
         b = ((torch.rand((k, n), generator=g, device=dev) * 2 - 1) / k ** 0.5).to(torch.bfloat16)
