@@ -102,52 +102,72 @@ __device__ __forceinline__ float exp2_acc(float x) {
 }
 
 // ---- pre-pass -----------------------------------------------------------------------------------
-// Rows of 64 floats (unit u at src + u*unit_stride) -> contiguous hi/lo planes [units, S, 64].
-// blockIdx.y = unit; four floats per thread when the unit start is 16-byte aligned.
-__global__ void split_rows_kernel(const float* __restrict__ src, long long unit_stride, float* __restrict__ hi,
-                                  float* __restrict__ lo, int seq) {
-  const int u = blockIdx.y;
+// Rows of 64 floats (unit u at src + u*unit_stride) -> contiguous hi/lo planes [units, S, 64],
+// by `nblk` blocks of 256 threads (block `bx`), four floats per thread when the unit start is
+// 16-byte aligned.
+__device__ __forceinline__ void split_rows(const float* __restrict__ src, long long unit_stride, float* __restrict__ hi,
+                                           float* __restrict__ lo, int seq, int u, int bx, int nblk) {
   const float* su = src + static_cast<long long>(u) * unit_stride;
   float* hu = hi + static_cast<long long>(u) * seq * D;
   float* lu = lo + static_cast<long long>(u) * seq * D;
   const int n = seq * D;
   if ((reinterpret_cast<uintptr_t>(su) & 15u) == 0) {
-    for (int i = (blockIdx.x * blockDim.x + threadIdx.x) * 4; i < n; i += gridDim.x * blockDim.x * 4) {
+    for (int i = (bx * 256 + static_cast<int>(threadIdx.x)) * 4; i < n; i += nblk * 256 * 4) {
       const float4 v = *reinterpret_cast<const float4*>(su + i);
       const float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
       *reinterpret_cast<float4*>(hu + i) = h;
       *reinterpret_cast<float4*>(lu + i) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
     }
   } else {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    for (int i = bx * 256 + static_cast<int>(threadIdx.x); i < n; i += nblk * 256) {
       const float v = su[i], h = tf32_round(v);
       hu[i] = h;
       lu[i] = v - h;
     }
   }
 }
-// V [units][S][64] (unit stride) -> hi/lo planes of V^T [units][64][Sp], zero for keys >= S.
-__global__ void split_vt_kernel(const float* __restrict__ v, long long unit_stride, float* __restrict__ hi_t,
-                                float* __restrict__ lo_t, int seq, int sp) {
-  __shared__ float tile[32][33];
-  const int u = blockIdx.z;
-  const int k0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+// One 32-key x 32-d tile of V [units][S][64] (unit stride) -> hi/lo planes of V^T [units][64][Sp],
+// zero for keys >= S, through shared memory (coalesced both ways).
+__device__ __forceinline__ void split_vt_tile(const float* __restrict__ v, long long unit_stride,
+                                              float* __restrict__ hi_t, float* __restrict__ lo_t, int seq, int sp,
+                                              int u, int k0, int d0, float (&tile)[32][33]) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const float* vu = v + static_cast<long long>(u) * unit_stride;
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+  for (int r = ty; r < 32; r += 8) {
     const int k = k0 + r;
-    tile[r][threadIdx.x] = k < seq ? vu[static_cast<long long>(k) * D + d0 + threadIdx.x] : 0.0f;
+    tile[r][tx] = k < seq ? vu[static_cast<long long>(k) * D + d0 + tx] : 0.0f;
   }
   __syncthreads();
   float* hu = hi_t + static_cast<long long>(u) * D * sp;
   float* lu = lo_t + static_cast<long long>(u) * D * sp;
-  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
-    const int d = d0 + r, k = k0 + threadIdx.x;
+  for (int r = ty; r < 32; r += 8) {
+    const int d = d0 + r, k = k0 + tx;
     if (k < sp) {
-      const float x = tile[threadIdx.x][r];
+      const float x = tile[tx][r];
       const float h = tf32_round(x);
       hu[static_cast<long long>(d) * sp + k] = h;
       lu[static_cast<long long>(d) * sp + k] = x - h;
     }
+  }
+}
+// The whole pre-pass in one launch (blockIdx.y = unit): blocks [0, nrb) split Q's rows, [nrb,
+// 2 nrb) K's rows (nrb = 0 when the caller supplies Q and K planes), the rest one V^T tile each.
+__global__ void __launch_bounds__(256) split_qkv_kernel(const float* __restrict__ q, long long q_stride,
+                                                        const float* __restrict__ k, long long k_stride,
+                                                        const float* __restrict__ v, long long v_stride,
+                                                        float* __restrict__ qh, float* __restrict__ ql,
+                                                        float* __restrict__ kh, float* __restrict__ kl,
+                                                        float* __restrict__ vh, float* __restrict__ vl, int seq,
+                                                        int sp, int nrb) {
+  __shared__ float tile[32][33];
+  const int u = blockIdx.y, bx = blockIdx.x;
+  if (bx < nrb) {
+    split_rows(q, q_stride, qh, ql, seq, u, bx, nrb);
+  } else if (bx < 2 * nrb) {
+    split_rows(k, k_stride, kh, kl, seq, u, bx - nrb, nrb);
+  } else {
+    const int t = bx - 2 * nrb;
+    split_vt_tile(v, v_stride, vh, vl, seq, sp, u, (t >> 1) * 32, (t & 1) * 32, tile);
   }
 }
 
@@ -627,14 +647,13 @@ cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, si
       return e;
     attr_set = true;
   }
-  const dim3 sgrid(static_cast<unsigned>(std::min<long long>((static_cast<long long>(a.seq) * D / 4 + 255) / 256, 64)),
-                   static_cast<unsigned>(a.units));
-  if (!qk_ready) {
-    split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.q), a.q_unit_stride, qh, ql, a.seq);
-    split_rows_kernel<<<sgrid, 256, 0, s>>>(static_cast<const float*>(a.k), a.k_unit_stride, kh, kl, a.seq);
-  }
-  split_vt_kernel<<<dim3((sp + 31) / 32, D / 32, a.units), dim3(32, 8), 0, s>>>(static_cast<const float*>(a.v),
-                                                                                a.v_unit_stride, vh, vl, a.seq, sp);
+  // One pre-pass launch: Q and K row splits (unless the caller wrote those planes) and V^T tiles.
+  const int nrb = qk_ready ? 0
+                           : static_cast<int>(std::min<long long>((static_cast<long long>(a.seq) * D / 4 + 255) / 256, 64));
+  const int nvt = ((sp + 31) / 32) * (D / 32);
+  split_qkv_kernel<<<dim3(static_cast<unsigned>(2 * nrb + nvt), static_cast<unsigned>(a.units)), 256, 0, s>>>(
+      static_cast<const float*>(a.q), a.q_unit_stride, static_cast<const float*>(a.k), a.k_unit_stride,
+      static_cast<const float*>(a.v), a.v_unit_stride, qh, ql, kh, kl, vh, vl, a.seq, sp, nrb);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   Params p;
   p.out = static_cast<float*>(a.out);
