@@ -23,12 +23,16 @@
 // Causal: only KV tiles at or below the diagonal are visited; per-element masks only on the
 // diagonal / sequence-tail tile.  CTAs run in groups of 16 units (heaviest Q tiles of the group
 // first), so a wave of CTAs shares the K/V of few units in L2 and the light tiles run last.
+// A persistent form of the same kernel (tune-cache name tcgen05_1qp) keeps two CTAs per SM
+// resident and lets each claim Q tiles from a global counter; it is exact but measured no faster
+// at config 3, so one CTA per Q tile stays the default.
 // All mbarrier waits are bounded (common.cuh).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <string>
 
 #include "../../include/lc_b200.h"
@@ -70,11 +74,14 @@ struct AttnTail {
   uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
   uint64_t drain;
   uint64_t o_staged;  // the 4 softmax warps have written the bf16 O tile into the Q buffer
+  uint64_t item_full[4];   // persistent form: item ring published by the Q/K producer thread
+  uint64_t item_empty[4];  // ... and released by the MMA warp, the V thread and 4 softmax warps
+  int item_slot[4];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-template <int D>
+template <int D, bool PERSIST>
 struct Layout {
   static constexpr int NCH = D / 64;                      // 64-column chunks per row
   static constexpr int Q_BYTES = NCH * CHUNK_BYTES;
@@ -83,14 +90,16 @@ struct Layout {
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
   static constexpr int V_OFF = K_OFF + K_STAGES * KV_BYTES;
   static constexpr int TAIL_OFF = V_OFF + V_STAGES * KV_BYTES;
-  // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel
-  // without static shared memory starts 1 KB-aligned; the kernel checks this and bails out
-  // with an error code otherwise.
+  // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel without static shared memory starts
+  // 1 KB-aligned; the kernel checks this and bails out with an error code otherwise.
   static constexpr size_t SMEM = TAIL_OFF + sizeof(AttnTail);
 };
 
+constexpr int kItemSlots = 4;
+
 struct FaParams {
   __nv_bfloat16* out;
+  unsigned* sched;  // persistent form: [next item counter, finished CTAs], zero at launch
   int units, seq, nq;  // nq = Q tiles per unit
   int group;           // causal CTA order: units per group, heaviest Q tiles of a group first
   int causal;
@@ -161,12 +170,55 @@ __device__ __forceinline__ void load_rows(uint8_t* dst, const CUtensorMap* map, 
   for (int c = 0; c < nch; ++c) tma_load_3d(dst + c * chunk_bytes, map, c * 64, row, unit, bar);
 }
 
-template <int D>
+// Item b (0 <= b < nq * units) -> (Q tile, unit).  Units are taken in groups of p.group; inside a
+// group the heaviest Q tiles of all its units come first.
+__device__ __forceinline__ void fa_item(const FaParams& p, int b, int& qt, int& unit) {
+  const int per_group = p.group * p.nq;
+  const int g = b / per_group, r = b % per_group;
+  const int gu = min(p.group, p.units - g * p.group);  // units in this (possibly short) group
+  qt = p.nq - 1 - r / gu;
+  unit = g * p.group + r % gu;
+}
+__device__ __forceinline__ int fa_kv_tiles(const FaParams& p, int qt) {
+  const int kv_tiles_all = (p.seq + TK - 1) / TK;
+  return p.causal ? min(kv_tiles_all, (qt * TILE + TILE - 1) / TK + 1) : kv_tiles_all;
+}
+
+// The CTA's it-th item: blockIdx.x alone without PERSIST; otherwise read from the item ring
+// (-1 = no more items).  Every reader releases the slot once it has the value.
+template <bool PERSIST>
+__device__ __forceinline__ bool fa_take_item(AttnTail* st, int it, int b0, int n_items, bool whole_warp,
+                                             volatile int* abort_flag, unsigned* err, unsigned code, int& b) {
+  if (!PERSIST) {
+    b = (it == 0 && b0 < n_items) ? b0 : -1;
+    return true;
+  }
+  const int r = it % kItemSlots;
+  const uint32_t par = (it / kItemSlots) & 1;
+  const bool ok = whole_warp ? warp_wait_poll(&st->item_full[r], par, abort_flag, err, code)
+                             : mbar_wait_bounded(&st->item_full[r], par, abort_flag, err, code);
+  if (!ok) return false;
+  b = *reinterpret_cast<volatile int*>(&st->item_slot[r]);
+  if (whole_warp) __syncwarp();
+  if (!whole_warp || (threadIdx.x & 31) == 0) mbar_arrive(&st->item_empty[r]);
+  return true;
+}
+
+// PERSIST = false: one CTA per item (grid = items), O staged in the idle Q buffer.
+// PERSIST = true: two resident CTAs per SM; each starts with item blockIdx.x and then claims the
+// next unclaimed item of the heavy-first order from a global counter (greedy, so the light items
+// fill the tail).  Its Q/K producer thread claims and publishes items to the other roles through
+// a 4-slot shared-memory ring.  The K/V rings, the TMEM score buffers and every barrier phase run
+// on a global KV-step counter across items, so the next item's K/V loads and first score MMA
+// overlap the previous item's last softmax and epilogue; the next Q is loaded as soon as the
+// previous item's last S MMA is done, and O is written from registers, so the Q buffer is never
+// needed for the epilogue.  This removes the per-CTA launch gap, set-up and cold Q wait.
+template <int D, bool PERSIST>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                   const FaParams p) {
-  using LY = Layout<D>;
+  using LY = Layout<D, PERSIST>;
   constexpr int NCH = LY::NCH;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // the 128-byte swizzle atoms need 1 KB alignment
@@ -181,19 +233,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Unit-major order (a wave shares the K/V of few units in L2), heaviest Q tile first inside a unit.
-  int qt, unit;
-  {
-    const int b = static_cast<int>(blockIdx.x);
-    const int per_group = p.group * p.nq;
-    const int g = b / per_group, r = b % per_group;
-    const int gu = min(p.group, p.units - g * p.group);  // units in this (possibly short) group
-    qt = p.nq - 1 - r / gu;
-    unit = g * p.group + r % gu;
-  }
-  const int q0 = qt * TILE;
-  const int kv_tiles_all = (p.seq + TK - 1) / TK;
-  const int n_kv = p.causal ? min(kv_tiles_all, (q0 + TILE - 1) / TK + 1) : kv_tiles_all;
+  const int n_items = p.nq * p.units;
+  const int b0 = static_cast<int>(blockIdx.x);
 
   if (threadIdx.x == 0) {
     mbar_init(&st->q_full, 1);
@@ -207,15 +248,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     mbar_init(&st->o_done[1], 1);
     mbar_init(&st->drain, 1);
     mbar_init(&st->o_staged, 4);
+    for (int r = 0; r < kItemSlots; ++r) {
+      mbar_init(&st->item_full[r], 1);
+      mbar_init(&st->item_empty[r], 6);
+    }
     st->abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
     tma_prefetch_desc(&map_v);
     tma_prefetch_desc(&map_o);
-    // The Q tile (a cold HBM read) is requested before the TMEM allocation and the CTA barrier.
-    mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
-    load_rows(sQ, &map_q, NCH, CHUNK_BYTES, q0, unit, &st->q_full);
+    // The first Q tile (a cold HBM read) is requested before the TMEM allocation and the CTA barrier.
+    if (b0 < n_items) {
+      int qt, unit;
+      fa_item(p, b0, qt, unit);
+      mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
+      load_rows(sQ, &map_q, NCH, CHUNK_BYTES, qt * TILE, unit, &st->q_full);
+    }
   }
   if (warp == 0) {
     tmem_alloc(&st->tmem_base, TMEM_COLS);
@@ -237,27 +286,80 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // ------------------------------------------------------------ TMA producer: Q and K
     if (lane == 0) {
       bool ok = true;
-      int k_issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int ks = j % K_STAGES;
-        if (j + K_STAGES < n_kv)  // warm L2 for the K tile that will take this slot next
-          for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + K_STAGES) * TK, unit);
-        // Slot ks last held K_{j-2}: S_{j-2} must have finished reading it.  Every MMA group has
-        // exactly one commit (S_j -> s_full[j&1]), and this thread observes S_0, S_1, ... in
-        // order, so each parity wait is unambiguous.
-        if (j >= K_STAGES && !mbar_wait_bounded(&st->s_full[(j - K_STAGES) & 1], ((j - K_STAGES) >> 1) & 1,
-                                                abort_flag, p.err_word, kErrAttnLoadWait)) {
+      int g = 0;        // global KV step = K loads issued
+      int q_loads = 1;  // Q tiles requested (the first one above)
+      // Publish item `it` (b < 0: none left) once every reader has released its ring slot.
+      auto publish = [&](int it, int b) -> bool {
+        const int r = it % kItemSlots;
+        if (it >= kItemSlots && !mbar_wait_bounded(&st->item_empty[r], ((it / kItemSlots) - 1) & 1, abort_flag,
+                                                    p.err_word, kErrAttnLoadWait))
+          return false;
+        st->item_slot[r] = b;
+        mbar_arrive(&st->item_full[r]);
+        return true;
+      };
+      for (int b = b0, it = 0; ok; ++it) {
+        if (PERSIST && !publish(it, b < n_items ? b : -1)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&st->k_full[ks], LY::KV_BYTES);
-        load_rows(sK + ks * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[ks]);
-        ++k_issued;
+        if (b >= n_items) break;
+        int qt, unit;
+        fa_item(p, b, qt, unit);
+        const int n_kv = fa_kv_tiles(p, qt);
+        int nxt = n_items;
+        for (int j = 0; j < n_kv; ++j) {
+          const int ks = g % K_STAGES;
+          // The next item is claimed a few KV steps before this item ends: late enough that claims
+          // follow the order CTAs run dry in (greedy balance), early enough that the atomic's
+          // latency is hidden.
+          if (PERSIST && j == (n_kv > 3 ? n_kv - 3 : 0)) nxt = static_cast<int>(gridDim.x + atomicAdd(p.sched, 1u));
+          if (PERSIST && j == n_kv - 1 && nxt < n_items) {
+            // Warm L2 with the next item's Q and first K/V tiles: their loads are issued at the
+            // item boundary and would otherwise be cold HBM reads on the critical path.
+            int nqt, nunit;
+            fa_item(p, nxt, nqt, nunit);
+            for (int c = 0; c < NCH; ++c) {
+              tma_prefetch_l2_3d(&map_q, c * 64, nqt * TILE, nunit);
+              tma_prefetch_l2_3d(&map_k, c * 64, 0, nunit);
+              tma_prefetch_l2_3d(&map_k, c * 64, TK, nunit);
+              tma_prefetch_l2_3d(&map_v, c * 64, 0, nunit);
+              tma_prefetch_l2_3d(&map_v, c * 64, TK, nunit);
+            }
+          }
+          if (j + K_STAGES < n_kv)  // warm L2 for the K tile that will take this slot next
+            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + K_STAGES) * TK, unit);
+          // Slot ks last held the K of global step g-2: that S MMA must have finished reading it.
+          // Every MMA group has exactly one commit (S_g -> s_full[g&1]), and this thread observes
+          // S_0, S_1, ... in order, so each parity wait is unambiguous.
+          if (g >= K_STAGES && !mbar_wait_bounded(&st->s_full[(g - K_STAGES) & 1], ((g - K_STAGES) >> 1) & 1,
+                                                  abort_flag, p.err_word, kErrAttnLoadWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&st->k_full[ks], LY::KV_BYTES);
+          load_rows(sK + ks * LY::KV_BYTES, &map_k, NCH, KCHUNK_BYTES, j * TK, unit, &st->k_full[ks]);
+          ++g;
+          if (PERSIST && it > 0 && j == 0) {
+            // This item's Q replaces the previous one once the previous item's last S MMA (global
+            // step g-2 now) is done; the next completion of that barrier needs this Q, so the
+            // parity wait is unambiguous.
+            if (!mbar_wait_bounded(&st->s_full[(g - 2) & 1], ((g - 2) >> 1) & 1, abort_flag, p.err_word,
+                                   kErrAttnLoadWait)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&st->q_full, LY::Q_BYTES);
+            load_rows(sQ, &map_q, NCH, CHUNK_BYTES, qt * TILE, unit, &st->q_full);
+            ++q_loads;
+          }
+        }
+        if (!PERSIST) break;
+        b = nxt;
       }
       if (!ok) {
-        drain(&st->q_full, 0);
-        for (int j = k_issued > K_STAGES ? k_issued - K_STAGES : 0; j < k_issued; ++j)
-          drain(&st->k_full[j % K_STAGES], (j / K_STAGES) & 1);
+        drain(&st->q_full, (q_loads - 1) & 1);
+        for (int x = g > K_STAGES ? g - K_STAGES : 0; x < g; ++x) drain(&st->k_full[x % K_STAGES], (x / K_STAGES) & 1);
       }
     }
   } else if (warp == 6) {
@@ -265,66 +367,86 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     // A separate thread, so a V slot that frees late never holds back the next K load.
     if (lane == 0) {
       bool ok = true;
-      int v_issued = 0;
-      for (int j = 0; j < n_kv; ++j) {
-        const int vs = j % V_STAGES;
-        if (j + V_STAGES < n_kv)
-          for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
-        // Slot vs last held V_{j-2}: PV_{j-2} (one commit: o_done[j%2]) must be done.  PV_j cannot
-        // complete before V_j is issued here, so the parity wait is unambiguous.
-        if (j >= V_STAGES && !mbar_wait_bounded(&st->o_done[(j - V_STAGES) % P_BUFS], ((j - V_STAGES) >> 1) & 1,
-                                                abort_flag, p.err_word, kErrAttnLoadWait)) {
+      int g = 0;  // global KV step = V loads issued
+      for (int it = 0; ok; ++it) {
+        int b;
+        if (!fa_take_item<PERSIST>(st, it, b0, n_items, false, abort_flag, p.err_word, kErrAttnLoadWait, b)) {
           ok = false;
           break;
         }
-        mbar_arrive_expect_tx(&st->v_full[vs], LY::KV_BYTES);
-        load_rows(sV + vs * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[vs]);
-        ++v_issued;
+        if (b < 0) break;
+        int qt, unit;
+        fa_item(p, b, qt, unit);
+        const int n_kv = fa_kv_tiles(p, qt);
+        for (int j = 0; j < n_kv; ++j) {
+          const int vs = g % V_STAGES;
+          if (j + V_STAGES < n_kv)
+            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
+          // Slot vs last held the V of step g-2: that PV (one commit: o_done[g%2]) must be done.
+          // PV_g cannot complete before V_g is issued here, so the parity wait is unambiguous.
+          if (g >= V_STAGES && !mbar_wait_bounded(&st->o_done[(g - V_STAGES) % P_BUFS], ((g - V_STAGES) >> 1) & 1,
+                                                  abort_flag, p.err_word, kErrAttnLoadWait)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&st->v_full[vs], LY::KV_BYTES);
+          load_rows(sV + vs * LY::KV_BYTES, &map_v, NCH, KCHUNK_BYTES, j * TK, unit, &st->v_full[vs]);
+          ++g;
+        }
       }
       if (!ok)
-        for (int j = v_issued > V_STAGES ? v_issued - V_STAGES : 0; j < v_issued; ++j)
-          drain(&st->v_full[j % V_STAGES], (j / V_STAGES) & 1);
+        for (int x = g > V_STAGES ? g - V_STAGES : 0; x < g; ++x) drain(&st->v_full[x % V_STAGES], (x / V_STAGES) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     // The whole warp runs the issue loop (waits polled by every lane) and one elected lane issues
     // each MMA, with descriptors advanced by constant adds.
-    {
-      constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TK, 0, 0);    // Q K-major, K K-major
-      constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);     // P (TMEM) K-major, V MN-major
-      const uint32_t q_addr = smem_u32(sQ);
-      bool ok = warp_wait_poll(&st->q_full, 0, abort_flag, p.err_word, kErrAttnMmaWait);
-      bool issued = false;
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % K_STAGES;
-        if (!warp_wait_poll(&st->k_full[s], (j / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
-          return false;
-        tc_fence_after();
-        const uint64_t qd = smem_desc_sw128(q_addr, 16, 1024);
-        const uint64_t kd = smem_desc_sw128(smem_u32(sK + s * LY::KV_BYTES), 16, 1024);
-        const uint32_t d_tmem = tmem + static_cast<uint32_t>((j & 1) * TK);
+    constexpr uint32_t IDESC_S = idesc_bf16_f32(TILE, TK, 0, 0);  // Q K-major, K K-major
+    constexpr uint32_t IDESC_O = idesc_bf16_f32(TILE, D, 0, 1);   // P (TMEM) K-major, V MN-major
+    const uint32_t q_addr = smem_u32(sQ);
+    bool ok = true, issued = false;
+    auto issue_s = [&](int gs) -> bool {  // S of global step gs into TMEM buffer gs&1
+      const int s = gs % K_STAGES;
+      if (!warp_wait_poll(&st->k_full[s], (gs / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
+        return false;
+      tc_fence_after();
+      const uint64_t qd = smem_desc_sw128(q_addr, 16, 1024);
+      const uint64_t kd = smem_desc_sw128(smem_u32(sK + s * LY::KV_BYTES), 16, 1024);
+      const uint32_t d_tmem = tmem + static_cast<uint32_t>((gs & 1) * TK);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t qo16 = ((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;  // address field: bytes / 16
-          const uint32_t ko16 = ((kk >> 2) * KCHUNK_BYTES + (kk & 3) * 32) >> 4;
-          umma_f16_ss_w(d_tmem, qd + qo16, kd + ko16, IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        issued = true;
-        umma_commit_w(&st->s_full[j & 1]);  // the only commit of this MMA group
-        return true;
-      };
-      if (ok) ok = issue_s(0);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t qo16 = ((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;  // address field: bytes / 16
+        const uint32_t ko16 = ((kk >> 2) * KCHUNK_BYTES + (kk & 3) * 32) >> 4;
+        umma_f16_ss_w(d_tmem, qd + qo16, kd + ko16, IDESC_S, kk > 0 ? 1u : 0u);
+      }
+      issued = true;
+      umma_commit_w(&st->s_full[gs & 1]);  // the only commit of this MMA group
+      return true;
+    };
+    int g = 0;  // global KV step of the item's first tile
+    for (int it = 0; ok; ++it) {
+      int b;
+      if (!fa_take_item<PERSIST>(st, it, b0, n_items, true, abort_flag, p.err_word, kErrAttnMmaWait, b)) {
+        ok = false;
+        break;
+      }
+      if (b < 0) break;
+      int qt, unit;
+      fa_item(p, b, qt, unit);
+      const int n_kv = fa_kv_tiles(p, qt);
+      // q_full completes once per item; the next Q needs this item's last S, so parity it&1 is unambiguous.
+      ok = warp_wait_poll(&st->q_full, it & 1, abort_flag, p.err_word, kErrAttnMmaWait) && issue_s(g);
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int s = j % V_STAGES;
-        if (j + 1 < n_kv && !issue_s(j + 1)) {
+        const int gg = g + j;
+        const int s = gg % V_STAGES;
+        if (j + 1 < n_kv && !issue_s(gg + 1)) {
           ok = false;
           break;
         }
-        // One barrier per TMEM buffer: p_full[j&1] next completes for P_{j+2}, which needs S_{j+2},
-        // issued only after this wait, so the parity wait is unambiguous.  (A single barrier
-        // waited with parity j&1 could already have completed P_j and P_{j+1}.)
-        if (!warp_wait_poll(&st->p_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !warp_wait_poll(&st->v_full[s], (j / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
+        // One barrier per TMEM buffer: p_full[gg&1] next completes for P_{gg+2}, which needs
+        // S_{gg+2}, issued only after this wait, so the parity wait is unambiguous.
+        if (!warp_wait_poll(&st->p_full[gg & 1], (gg >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !warp_wait_poll(&st->v_full[s], (gg / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
           ok = false;
           break;
         }
@@ -333,145 +455,162 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         const uint32_t o_tmem = tmem + 2 * TK;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
-          // A = P_j in TMEM (lanes = rows, 2 keys per column): +8 columns per 16 keys.  B = V,
-          // MN-major: 64-column d chunks 8 KB apart (LBO), +16 key rows * 128 B per step.
-          const uint32_t a_tmem = tmem + static_cast<uint32_t>((j % P_BUFS) * TK + kk * 8);
+          // A = P in TMEM (lanes = rows, 2 keys per column): +8 columns per 16 keys.  B = V,
+          // MN-major: 64-column d chunks 8 KB apart (LBO), +16 key rows * 128 B per step.  The
+          // item's first PV overwrites O, which the softmax warps read out (previous item's
+          // epilogue) before they hand over this item's first P.
+          const uint32_t a_tmem = tmem + static_cast<uint32_t>((gg % P_BUFS) * TK + kk * 8);
           umma_f16_ts_w(o_tmem, a_tmem, vd + (kk * 2048 >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit_w(&st->o_done[j % P_BUFS]);  // the only commit of this MMA group
+        umma_commit_w(&st->o_done[gg % P_BUFS]);  // the only commit of this MMA group
       }
-      if (!ok && issued) {
-        umma_commit_w(&st->drain);
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
-        }
+      g += n_kv;
+    }
+    if (!ok && issued) {
+      umma_commit_w(&st->drain);
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&st->drain, 0) && globaltimer_ns() - t0 < 100000000ull) {
       }
     }
   } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ softmax + epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // row within the Q tile == TMEM lane
-    const int qrow = q0 + row;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t o_tmem = tmem + lane_base + 2 * TK;
-    float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait_poll(&st->s_full[j & 1], (j >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+    int g = 0;        // global KV step of the item's first tile
+    for (int it = 0; ok; ++it) {
+      int b;
+      if (!fa_take_item<PERSIST>(st, it, b0, n_items, true, abort_flag, p.err_word, kErrAttnSoftmaxWait, b)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      // Both 32-column score loads in flight before a single wait.
-      uint32_t r[TK / 32][32];
-      {
-        const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TK);
-#pragma unroll
-        for (int c = 0; c < TK / 32; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
-        tmem_wait_ld();
-      }
-      const int kv0 = j * TK;
-      // Keys allowed for this row: k < seq, and k <= qrow when causal.
-      const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
-      if (kv0 + TK - 1 > kmax) {
-#pragma unroll
-        for (int e = 0; e < TK; ++e)
-          if (kv0 + e > kmax) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
-      }
-      // Row max: 8 independent partial maxima fed two scores per 3-input max, in raw score
-      // units (scale > 0, so max(s)*scale == max(s*scale)).
-      float pm[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(r[0][a]);
-#pragma unroll
-      for (int e = 8; e < TK; e += 2)
-        pm[(e >> 1) & 7] = max3(pm[(e >> 1) & 7], __uint_as_float(r[e >> 5][e & 31]),
-                                __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31]));
-      const float mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
-                       p.scale_log2;
-      // P_j overwrites S_j in place.  The last reader of those columns before S_j was PV_{j-2},
-      // issued before S_j by the same thread; s_full[j&1] therefore already covers it.
-      const bool need = mx > m + RESCALE_THRESHOLD;
-      float factor = 1.0f;
-      if (need) {
-        factor = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
-        l *= factor;
-        m = mx;
-      }
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // O is rescaled in place: PV_{j-1} must have landed first.
-        if (!warp_wait_poll(&st->o_done[(j - 1) % P_BUFS], ((j - 1) >> 1) & 1, abort_flag, p.err_word,
-                       kErrAttnCorrectionWait)) {
+      if (b < 0) break;
+      int qt, unit;
+      fa_item(p, b, qt, unit);
+      const int n_kv = fa_kv_tiles(p, qt);
+      const int q0 = qt * TILE;
+      const int qrow = q0 + row;
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < n_kv; ++j) {
+        const int gg = g + j;
+        if (!warp_wait_poll(&st->s_full[gg & 1], (gg >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < D; c += 16) {
-          uint32_t o[16];
-          tmem_ld16(o_tmem + c, o);
+        // Both 32-column score loads in flight before a single wait.
+        uint32_t r[TK / 32][32];
+        {
+          const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((gg & 1) * TK);
+#pragma unroll
+          for (int c = 0; c < TK / 32; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
           tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
-          tmem_st16(o_tmem + c, o);
         }
+        const int kv0 = j * TK;
+        // Keys allowed for this row: k < seq, and k <= qrow when causal.
+        const int kmax = p.causal ? min(qrow, p.seq - 1) : p.seq - 1;
+        if (kv0 + TK - 1 > kmax) {
+#pragma unroll
+          for (int e = 0; e < TK; ++e)
+            if (kv0 + e > kmax) r[e >> 5][e & 31] = __float_as_uint(-INFINITY);
+        }
+        // Row max: 8 independent partial maxima fed two scores per 3-input max, in raw score
+        // units (scale > 0, so max(s)*scale == max(s*scale)).
+        float pm[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) pm[a] = __uint_as_float(r[0][a]);
+#pragma unroll
+        for (int e = 8; e < TK; e += 2)
+          pm[(e >> 1) & 7] = max3(pm[(e >> 1) & 7], __uint_as_float(r[e >> 5][e & 31]),
+                                  __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31]));
+        const float mx = max3(max3(pm[0], pm[1], pm[2]), max3(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])) *
+                         p.scale_log2;
+        // P overwrites S in place.  The last reader of those columns before S_gg was PV_{gg-2},
+        // issued before S_gg by the same thread; s_full[gg&1] therefore already covers it.
+        const bool need = mx > m + RESCALE_THRESHOLD;
+        float factor = 1.0f;
+        if (need) {
+          factor = (m == -INFINITY) ? 0.0f : exp2f(m - mx);
+          l *= factor;
+          m = mx;
+        }
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          // O is rescaled in place: PV_{gg-1} must have landed first.
+          if (!warp_wait_poll(&st->o_done[(gg - 1) % P_BUFS], ((gg - 1) >> 1) & 1, abort_flag, p.err_word,
+                              kErrAttnCorrectionWait)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll 1
+          for (int c = 0; c < D; c += 16) {
+            uint32_t o[16];
+            tmem_ld16(o_tmem + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * factor);
+            tmem_st16(o_tmem + c, o);
+          }
+          tmem_wait_st();
+        }
+        // p = exp2(s*scale - m), one FFMA + ex2 each; m is finite here (key 0 <= qrow is always
+        // visible, so the first tile sets it).  Packed partial sums keep the adds independent.
+        const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
+        uint64_t ps2[4] = {0, 0, 0, 0};
+        const uint32_t p_tmem = tmem + lane_base + static_cast<uint32_t>((gg & 1) * TK);
+#pragma unroll
+        for (int gq = 0; gq < TK / 32; ++gq) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int e = gq * 32 + 2 * i;
+            // x = s*scale - m for two scores at once; masked scores are -inf, so ex2 gives 0.
+            float x0, x1;
+            unpk2(fma2(pk2(__uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31])),
+                       sc2, nm2),
+                  x0, x1);
+            const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+            ps2[i & 3] = add2(ps2[i & 3], pk2(e0, e1));
+            w[i] = pack_bf16x2(e0, e1);
+          }
+          tmem_st16(p_tmem + gq * 16, w);
+        }
+        float sum;
+        {
+          const uint64_t t = add2(add2(ps2[0], ps2[1]), add2(ps2[2], ps2[3]));
+          float a, c;
+          unpk2(t, a, c);
+          sum = a + c;
+        }
+        l += sum;
         tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st->p_full[gg & 1]);
       }
-      // p = exp2(s*scale - m), one FFMA + ex2 each; m is finite here (key 0 <= qrow is always
-      // visible, so the first tile sets it).  8 partial sums keep the adds independent.
-      const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
-      uint64_t ps2[4] = {0, 0, 0, 0};  // 4 independent packed partial sums
-      const uint32_t p_tmem = tmem + lane_base + static_cast<uint32_t>((j & 1) * TK);
-#pragma unroll
-      for (int g = 0; g < TK / 32; ++g) {
-        uint32_t w[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int e = g * 32 + 2 * i;
-          // x = s*scale - m for two scores at once; masked scores are -inf, so ex2 gives 0.
-          float x0, x1;
-          unpk2(fma2(pk2(__uint_as_float(r[e >> 5][e & 31]), __uint_as_float(r[(e + 1) >> 5][(e + 1) & 31])),
-                     sc2, nm2),
-                x0, x1);
-          const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
-          ps2[i & 3] = add2(ps2[i & 3], pk2(e0, e1));
-          w[i] = pack_bf16x2(e0, e1);
-        }
-        tmem_st16(p_tmem + g * 16, w);
-      }
-      float sum;
-      {
-        const uint64_t t = add2(add2(ps2[0], ps2[1]), add2(ps2[2], ps2[3]));
-        float a, b;
-        unpk2(t, a, b);
-        sum = a + b;
-      }
-      l += sum;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&st->p_full[j & 1]);
-    }
-    // The last two PVs (one per P buffer) must have landed in O.
-    if (ok && n_kv >= 2)
-      ok = warp_wait_poll(&st->o_done[(n_kv - 2) % P_BUFS], ((n_kv - 2) >> 1) & 1, abort_flag, p.err_word,
-                     kErrAttnCorrectionWait);
-    if (ok && warp_wait_poll(&st->o_done[(n_kv - 1) % P_BUFS], ((n_kv - 1) >> 1) & 1, abort_flag, p.err_word,
-                        kErrAttnCorrectionWait)) {
+      if (!ok) break;
+      // The last two PVs (one per P buffer) must have landed in O.  The next completion of either
+      // barrier needs a P of the next item, which these warps have not handed over yet.
+      const int gl = g + n_kv - 1;
+      if (n_kv >= 2)
+        ok = warp_wait_poll(&st->o_done[(gl - 1) % P_BUFS], ((gl - 1) >> 1) & 1, abort_flag, p.err_word,
+                            kErrAttnCorrectionWait);
+      if (ok)
+        ok = warp_wait_poll(&st->o_done[gl % P_BUFS], (gl >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait);
+      if (!ok) break;
       tc_fence_after();
-      // Epilogue: O / l (+ postprocess) as bf16 into the Q buffer, which no MMA reads any more
-      // (every S MMA completed before the last P.V), in the 128-byte-swizzled layout of the Q
-      // tile (16-byte chunk k of row r at chunk k ^ (r & 7): conflict-free), then one TMA store
-      // per 64-column box.  Rows past the sequence end are clipped by the tensor map.
       const float inv = 1.0f / l;
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(o_tmem + c, r);
+      // O / l (+ postprocess) as bf16 pairs, 32 columns at a time, into a 128-byte-swizzled
+      // [128 rows x 64 cols] box (16-byte chunk k of row r at chunk k ^ (r & 7): conflict-free).
+      auto stage32 = [&](int c, uint8_t* box) {
+        uint32_t rr[32];
+        tmem_ld32(o_tmem + c, rr);
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float y0 = __uint_as_float(r[2 * e]) * inv, y1 = __uint_as_float(r[2 * e + 1]) * inv;
+          float y0 = __uint_as_float(rr[2 * e]) * inv, y1 = __uint_as_float(rr[2 * e + 1]) * inv;
           if (p.post) {
             y0 = y0 * p.post_scale + p.post_bias;
             y1 = y1 * p.post_scale + p.post_bias;
@@ -482,23 +621,62 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
           }
           w[e] = pack_bf16x2(y0, y1);
         }
-        uint8_t* srow = sQ + (c >> 6) * CHUNK_BYTES + row * 128;
+        uint8_t* srow = box + row * 128;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int ch = ((c & 63) >> 3) + i;
           *reinterpret_cast<uint4*>(srow + ((ch ^ (row & 7)) << 4)) =
               make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
+      };
+      if constexpr (!PERSIST) {
+        // The Q buffer is idle (every S MMA completed before the last P.V): stage the whole tile
+        // there and write it with one TMA store per 64-column box.  Rows past the sequence end
+        // are clipped by the tensor map.
+#pragma unroll
+        for (int c = 0; c < D; c += 32) stage32(c, sQ + (c >> 6) * CHUNK_BYTES);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&st->o_staged);
+        if (warp == 2 && lane == 0 &&
+            mbar_wait_bounded(&st->o_staged, 0, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
+          for (int c = 0; c < NCH; ++c) tma_store_3d(&map_o, sQ + c * CHUNK_BYTES, c * 64, q0, unit);
+          bulk_commit_group();
+          bulk_wait_group_read0();  // shared memory must outlive the store's reads
+        }
+      } else {
+        // Straight from registers: each thread writes its own row (256 contiguous bytes at
+        // head_dim 128) with 16-byte stores that nothing waits for, so these warps go on to the
+        // next item's scores at once.  tcgen05.ld is warp-collective, so every lane loads and
+        // only the stores of rows past the sequence end are skipped.
+        uint4* orow = reinterpret_cast<uint4*>(p.out + (static_cast<size_t>(unit) * p.seq + qrow) * D);
+        const bool row_ok = qrow < p.seq;
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          uint32_t rr[32];
+          tmem_ld32(o_tmem + c, rr);
+          uint32_t w[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float y0 = __uint_as_float(rr[2 * e]) * inv, y1 = __uint_as_float(rr[2 * e + 1]) * inv;
+            if (p.post) {
+              y0 = y0 * p.post_scale + p.post_bias;
+              y1 = y1 * p.post_scale + p.post_bias;
+              if (p.post_relu) {
+                y0 = fmaxf(y0, 0.0f);
+                y1 = fmaxf(y1, 0.0f);
+              }
+            }
+            w[e] = pack_bf16x2(y0, y1);
+          }
+          if (row_ok)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              orow[c / 8 + i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+        tc_fence_before();  // these reads of O are ordered before the next item's first P hand-off
       }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&st->o_staged);
-      if (warp == 2 && lane == 0 &&
-          mbar_wait_bounded(&st->o_staged, 0, abort_flag, p.err_word, kErrAttnCorrectionWait)) {
-        for (int c = 0; c < NCH; ++c) tma_store_3d(&map_o, sQ + c * CHUNK_BYTES, c * 64, q0, unit);
-        bulk_commit_group();
-        bulk_wait_group_read0();  // shared memory must outlive the store's reads
-      }
+      g += n_kv;
     }
   }
 
@@ -507,6 +685,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
+  }
+  if (PERSIST && threadIdx.x == 0) {
+    // Every fetch of this CTA precedes this count, so the last CTA to finish can zero both words
+    // for the next launch that uses this counter slot.
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1u) == gridDim.x - 1) {
+      atomicExch(p.sched, 0u);
+      atomicExch(p.sched + 1, 0u);
+    }
   }
 }
 
@@ -934,6 +1121,7 @@ cudaError_t launch_fa2q(const AttnArgs& a, cudaStream_t s) {
     attr_set = true;
   }
   FaParams p;
+  p.sched = nullptr;
   p.out = static_cast<__nv_bfloat16*>(a.out);
   p.units = a.units;
   p.seq = a.seq;
@@ -953,7 +1141,7 @@ cudaError_t launch_fa2q(const AttnArgs& a, cudaStream_t s) {
 }
 
 
-template <int D>
+template <int D, bool PERSIST>
 cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
@@ -963,10 +1151,10 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   static bool attr_set = false;  // benign race: idempotent
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(Layout<D>::SMEM));
+    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(Layout<D, PERSIST>::SMEM));
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(fa_fwd_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -983,9 +1171,13 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   p.post_relu = a.post_relu;
   p.post = !(a.post_scale == 1.0f && a.post_bias == 0.0f && !a.post_relu);
   p.err_word = ctx->err_word;
-  const long long blocks = static_cast<long long>(p.nq) * a.units;
-  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  fa_fwd_kernel<D><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D>::SMEM, s>>>(mq, mk, mv, mo, p);
+  p.sched = PERSIST ? ctx->take_sched() : nullptr;
+  const long long items = static_cast<long long>(p.nq) * a.units;
+  if (items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  // Persistent form: two resident CTAs per SM.
+  const long long blocks = PERSIST ? std::min<long long>(items, 2LL * std::max(ctx->sm_count, 1)) : items;
+  fa_fwd_kernel<D, PERSIST><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D, PERSIST>::SMEM, s>>>(
+      mq, mk, mv, mo, p);
   return cudaGetLastError();
 }
 
@@ -1006,7 +1198,11 @@ cudaError_t attention_bf16_by_name(const AttnArgs& a, const std::string& name, c
   }
   if (name == kAttnTc1qName) {
     if (!attention_bf16_tc_supported(a)) return cudaErrorNotSupported;
-    return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+    return a.d == 64 ? launch_fa<64, false>(a, s) : launch_fa<128, false>(a, s);
+  }
+  if (name == kAttnTc1qPName) {
+    if (!attention_bf16_tc_supported(a)) return cudaErrorNotSupported;
+    return a.d == 64 ? launch_fa<64, true>(a, s) : launch_fa<128, true>(a, s);
   }
   if (name == "simt") return attention_bf16_simt(a, s);
   return cudaErrorInvalidValue;
@@ -1019,10 +1215,12 @@ cudaError_t attention_bf16(const AttnArgs& a, cudaStream_t s) {
   if (!forced_simt && attention_bf16_tc_supported(a)) {
     // Two Q tiles per CTA for head_dim 128 without a causal mask (0.248 vs 0.264 ms at
     // [128, 2048, 128]); causal stays on the one-tile kernel, whose 64-key diagonal tiles
-    // waste less (0.166 vs 0.174 ms).  The tune cache can pin either.
-    const bool two_q = cfg == kAttnTc2qName || (cfg != kAttnTc1qName && !a.causal);
-    if (a.d == 128 && two_q) return launch_fa2q(a, s);
-    return a.d == 64 ? launch_fa<64>(a, s) : launch_fa<128>(a, s);
+    // waste less (0.153 vs 0.164 ms), with one CTA per Q tile (the persistent form measured
+    // 0.154-0.156 ms at config 3).  The tune cache can pin any of the three.
+    if (cfg == kAttnTc1qName) return a.d == 64 ? launch_fa<64, false>(a, s) : launch_fa<128, false>(a, s);
+    if (cfg == kAttnTc1qPName) return a.d == 64 ? launch_fa<64, true>(a, s) : launch_fa<128, true>(a, s);
+    if (a.d == 128 && (cfg == kAttnTc2qName || !a.causal)) return launch_fa2q(a, s);
+    return a.d == 64 ? launch_fa<64, false>(a, s) : launch_fa<128, false>(a, s);
   }
   return attention_bf16_simt(a, s);
 }

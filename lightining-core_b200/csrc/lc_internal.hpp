@@ -6,6 +6,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -16,6 +17,13 @@ struct DeviceCtx {
   int device = -1;
   int sm_count = 0;
   unsigned* err_word = nullptr;  // device word written by kernels whose bounded waits gave up
+  // Work counters of persistent kernels: kSchedSlots pairs of words, zero between launches (each
+  // launch's last CTA zeroes its pair).  A launch takes the next pair in turn, so launches in
+  // flight at the same time on different streams use different pairs (up to kSchedSlots).
+  static constexpr int kSchedSlots = 64;
+  unsigned* sched = nullptr;
+  std::atomic<unsigned> sched_next{0};
+  unsigned* take_sched() { return sched + 2 * (sched_next.fetch_add(1, std::memory_order_relaxed) % kSchedSlots); }
   // Stream-ordered pool for per-call workspaces (the 3xTF32 split planes): a call allocates on its
   // own stream and frees on it after its kernels, so calls on different streams never wait for
   // each other and no lock is held on the launch path.  Freed memory stays cached in the pool.
@@ -154,6 +162,7 @@ bool attention_bf16_tc_supported(const AttnArgs& a);
 // tiles (two CTAs per SM), and two Q tiles per CTA with 128-key tiles (head_dim 128).
 constexpr const char* kAttnTc1qName = "tcgen05_1q";
 constexpr const char* kAttnTc2qName = "tcgen05_2q";
+constexpr const char* kAttnTc1qPName = "tcgen05_1qp";  // one-tile kernel, persistent CTAs
 // Strict fp32 attention on tcgen05 (3xTF32) by its tune-cache name.
 constexpr const char* kAttnTf32x3Name = "tcgen05_3xtf32";
 // Runs one bf16 attention kernel by its tune-cache name ("tcgen05_1q", "tcgen05_2q", "simt")

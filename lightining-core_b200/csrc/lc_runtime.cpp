@@ -128,17 +128,21 @@ DeviceCtx* device_ctx() {
   if (g_ctx[dev]) return g_ctx[dev];
   c = new DeviceCtx();
   c->device = dev;
+  // One allocation: the error word, padding to 256 bytes, then the persistent-kernel counters.
+  constexpr size_t kCtxWords = 64 + 2 * DeviceCtx::kSchedSlots;
   cudaMemPoolProps props = {};
   props.allocType = cudaMemAllocationTypePinned;
   props.location.type = cudaMemLocationTypeDevice;
   props.location.id = dev;
   if (cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-      cudaMalloc(&c->err_word, sizeof(unsigned)) != cudaSuccess ||
-      cudaMemset(c->err_word, 0, sizeof(unsigned)) != cudaSuccess || cudaMemPoolCreate(&c->pool, &props) != cudaSuccess) {
+      cudaMalloc(&c->err_word, kCtxWords * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemset(c->err_word, 0, kCtxWords * sizeof(unsigned)) != cudaSuccess ||
+      cudaMemPoolCreate(&c->pool, &props) != cudaSuccess) {
     if (c->err_word) cudaFree(c->err_word);
     delete c;
     return nullptr;
   }
+  c->sched = c->err_word + 64;
   uint64_t keep = ~0ull;  // keep freed workspace cached in the pool instead of returning it
   cudaMemPoolSetAttribute(c->pool, cudaMemPoolAttrReleaseThreshold, &keep);
   g_ctx[dev] = c;

@@ -334,6 +334,7 @@ lcError_t lcAttentionAutotune(const void* q, const void* k, const void* v, void*
     if (attention_f32_tc_supported(a)) cands.push_back(kAttnTf32x3Name);
   } else if (attention_bf16_tc_supported(a)) {
     cands.push_back(kAttnTc1qName);
+    cands.push_back(kAttnTc1qPName);
     if (head_dim == 128) cands.push_back(kAttnTc2qName);
   }
   cands.push_back("simt");

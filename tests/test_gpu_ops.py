@@ -69,13 +69,14 @@ def test_attention_bf16_shapes(gpu, units, s, d, causal):
     close_enough(ref, gpu.from_bf16(out), 2e-2, 2e-2)
 
 
-@pytest.mark.parametrize("kernel", ["tcgen05_1q", "tcgen05_2q"])
+@pytest.mark.parametrize("kernel", ["tcgen05_1q", "tcgen05_1qp", "tcgen05_2q"])
 @pytest.mark.parametrize("units,s,causal", [(1, 256, 0), (1, 256, 1), (2, 100, 1), (3, 777, 0), (2, 1000, 1),
-                                            (1, 300, 0), (1, 4100, 0)])
+                                            (1, 300, 0), (1, 4100, 0), (40, 1024, 1)])
 def test_attention_bf16_each_tc_kernel(gpu, kernel, units, s, causal):
-    """Both bf16 tensor-core attention kernels for head_dim 128 (one Q tile per CTA with 64-key
-    tiles; two Q tiles per CTA with 128-key tiles), pinned through the tune cache, on ragged and
-    short sequences (a second Q tile wholly past the end included)."""
+    """Every bf16 tensor-core attention kernel for head_dim 128 (one Q tile per CTA with 64-key
+    tiles; the same with persistent CTAs walking several Q tiles each; two Q tiles per CTA with
+    128-key tiles), pinned through the tune cache, on ragged and short sequences (a second Q tile
+    wholly past the end included) and on a shape with more Q tiles than resident CTAs."""
     rng = np.random.default_rng(units * 31 + s + causal)
     q, k, v = (P.bf16_round(rng.standard_normal((units, s, 128)).astype(np.float32)) for _ in range(3))
     gpu.tune_cache_set(gpu.TUNE_ATTENTION, s, 128, causal, kernel, gpu.BF16)
@@ -83,7 +84,7 @@ def test_attention_bf16_each_tc_kernel(gpu, kernel, units, s, causal):
         out = gpu.attention_batched(bf(gpu, q), bf(gpu, k), bf(gpu, v), bool(causal), gpu.BF16)
     finally:
         gpu.tune_cache_reset(gpu.TUNE_ATTENTION)
-    units_checked = range(units) if s <= 1000 else [0]
+    units_checked = range(units) if s <= 1000 and units <= 3 else [0, units - 1]
     for u in units_checked:
         rows = slice(0, s) if s <= 1000 else slice(s - 300, s)
         ref = P.attention_rows(q[u], k[u], v[u], bool(causal), rows.start, rows.stop)

@@ -117,7 +117,7 @@ def test_attention_autotune_records_and_is_used(gpu, dtype, d, causal):
     dout = gpu.DeviceBuffer(units * seq * d * (4 if dt == gpu.F32 else 2))
     try:
         best = gpu.attention_autotune(dq, dk, dv, dout, units, seq, d, bool(causal), dt)
-        allowed = {"simt", "tcgen05_3xtf32"} if dt == gpu.F32 else {"simt", "tcgen05_1q", "tcgen05_2q"}
+        allowed = {"simt", "tcgen05_3xtf32"} if dt == gpu.F32 else {"simt", "tcgen05_1q", "tcgen05_1qp", "tcgen05_2q"}
         assert best in allowed
         assert best != "tcgen05_2q" or d == 128
         assert gpu.tune_cache_get(gpu.TUNE_ATTENTION, seq, d, causal, dt) == best
