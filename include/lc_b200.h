@@ -343,7 +343,7 @@ lcError_t lcMatMulSessionRunBatch(lcMatMulSession_t s, const void* a, const void
 /* CSV `#lc_tune_cache,<matmul|attention>,2` + `#columns,...`; keys (m,k,n,dtype) for matmul and
  * (seq,head_dim,causal,dtype) for attention; values are sm_100a kernel configuration names
  * (matmul: "simt128x128", "simt128x64", "simt64x64", "tcgen05_128x256", "tcgen05_2sm_256x256",
- * "tcgen05_3xtf32", "simt"; attention: "tcgen05_1q", "tcgen05_2q", "tcgen05_3xtf32", "simt").  A NULL path
+ * "tcgen05_3xtf32", "simt"; attention: "tcgen05_1q", "tcgen05_1qp", "tcgen05_2q", "tcgen05_3xtf32", "simt").  A NULL path
  * means CJ_MATMUL_TUNE_CACHE_FILE / CJ_ATTN_TUNE_CACHE_FILE, which is also loaded on first use and
  * rewritten whenever an entry is added.  Load rejects a file with an unknown header
  * (LC_NOT_SUPPORTED) and keeps the current rows. */
