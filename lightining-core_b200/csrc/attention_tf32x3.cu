@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(256) split_qkv_kernel(const float* __restrict_
                                                         float* __restrict__ kh, float* __restrict__ kl,
                                                         float* __restrict__ vh, float* __restrict__ vl, int seq,
                                                         int sp, int nrb) {
+  griddep_launch_dependents();  // the attention may take its SMs now; it waits for these planes itself
   __shared__ float tile[32][33];
   const int u = blockIdx.y, bx = blockIdx.x;
   if (bx < nrb) {
@@ -184,6 +185,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   auto sK = [&](int stage, int lo) { return smem + K_OFF + (stage * 2 + lo) * K_PLANE; };
   auto sV = [&](int stage, int lo) { return smem + V_OFF + (stage * 2 + lo) * V_PLANE; };
 
+  griddep_wait();  // Q/K/V planes come from the split pre-pass (or the conv epilogue)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int qt = p.nq - 1 - static_cast<int>(blockIdx.x) % p.nq;
@@ -672,8 +674,8 @@ cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, si
   p.err_word = ctx->err_word;
   const long long grid = static_cast<long long>(p.nq) * a.units;
   if (grid > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  fa_f32_tc_kernel<<<static_cast<unsigned>(grid), NUM_THREADS, SMEM_BYTES, s>>>(mqh, mql, mkh, mkl, mvh, mvl, p);
-  return cudaGetLastError();
+  return launch_pdl(fa_f32_tc_kernel, dim3(static_cast<unsigned>(grid)), dim3(NUM_THREADS), SMEM_BYTES, s, mqh, mql,
+                    mkh, mkl, mvh, mvl, p);
 }
 
 }  // namespace lcb

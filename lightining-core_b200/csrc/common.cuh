@@ -12,11 +12,39 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #ifndef LC_WAIT_TIMEOUT_NS
 #define LC_WAIT_TIMEOUT_NS 2000000000ull  // 2 s
 #endif
 
 namespace lcb {
+
+// ---- programmatic dependent launch -------------------------------------------------------------
+// A pre-pass kernel lets the kernel launched after it on the same stream (with launch_pdl) become
+// resident early; that kernel calls griddep_wait() before it touches anything the pre-pass
+// writes, which returns once the pre-pass grid has completed and its writes are visible.  In a
+// kernel launched normally griddep_wait() returns at once.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 
 // Error-word codes (low byte = site, upper bits = kernel id).
 enum : unsigned {

@@ -364,6 +364,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::NUM_THREADS, 
   tc_fence_before();
   cluster_sync_all();  // barrier inits and the TMEM allocation visible to both CTAs
   tc_fence_after();
+  griddep_wait();  // the split planes of x come from the pre-pass
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
 
@@ -556,6 +557,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairk::NUM_THREADS, 
 // 32 channels x 32 pixels of one image per block through shared memory, coalesced both ways.
 __global__ void nchw_to_nhwc_split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
                                           int c, int pix) {
+  griddep_launch_dependents();  // the conv may take its SMs now; it waits for these planes itself
   __shared__ float tile[32][33];
   const int n = blockIdx.z, c0 = blockIdx.y * 32, p0 = blockIdx.x * 32;
   const float* xn = x + static_cast<long long>(n) * c * pix;
@@ -774,14 +776,15 @@ cudaError_t conv_implicit_run(const float* x, const float* w, const float* bias,
       const long long tiles = (pixels + 2 * BM - 1) / (2 * BM);
       const int max_clusters = ctx->sm_count / 2;
       const int clusters = static_cast<int>(tiles < max_clusters ? tiles : max_clusters);
-      conv_im2col_pair_kernel<<<2 * clusters, pairk::NUM_THREADS, psmem, s>>>(mhi, mlo, mxhi, mxlo, p, nst);
+      e = launch_pdl(conv_im2col_pair_kernel, dim3(2 * clusters), dim3(pairk::NUM_THREADS), psmem, s, mhi, mlo, mxhi,
+                     mxlo, p, nst);
     } else {
       const long long tiles = (pixels + BM - 1) / BM;
       const int grid = static_cast<int>(tiles < ctx->sm_count ? tiles : ctx->sm_count);
       const size_t smem = 1024 + STAGES * (2 * A_PLANE_BYTES + 2 * static_cast<size_t>(out_c) * BK * 4) + sizeof(Tail);
       conv_implicit_tf32x3_kernel<<<grid, NUM_THREADS, smem, s>>>(mhi, mlo, p);
+      e = cudaGetLastError();
     }
-    e = cudaGetLastError();
   }
   if (xws) {
     const cudaError_t ex = workspace_free(xws, s);

@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(256) tf32_matmul_prep_kernel(const float4* __r
                                                                float* __restrict__ bl_t, int K, int N, int bt_x,
                                                                unsigned* __restrict__ counters, int n_counters) {
   __shared__ float tile[32][33];
+  griddep_launch_dependents();  // the GEMM may take its SMs now; it waits for these planes itself
   const int bid = static_cast<int>(blockIdx.x);
   if (bid == 0)
     for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0u;
@@ -536,6 +537,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(pairg::Cfg<BN>::THRE
   tc_fence_before();
   cluster_sync_all();  // barrier inits and the TMEM allocation visible to both CTAs
   tc_fence_after();
+  griddep_wait();  // the split planes and counters come from the pre-pass
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
 
@@ -892,10 +894,9 @@ cudaError_t launch_pair_bn(const CUtensorMap& mah, const CUtensorMap& mal, const
   }
   const int items = pl.tiles * pl.ksplit;
   const int clusters = items < clusters_max ? items : clusters_max;
-  gemm_tf32x3_pair_kernel<BN><<<2 * clusters, pairg::Cfg<BN>::THREADS, pairg::smem_bytes<BN>(), s>>>(
-      mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride, epi.row_stride, epi.row_bias, epi.relu,
-      pl.ksplit, pl.kb_per, part, counters, err_word);
-  return cudaGetLastError();
+  return launch_pdl(gemm_tf32x3_pair_kernel<BN>, dim3(2 * clusters), dim3(pairg::Cfg<BN>::THREADS),
+                    pairg::smem_bytes<BN>(), s, mah, mal, pbh, pbl, epi.c, m, n, kp, epi.period, epi.batch_stride,
+                    epi.row_stride, epi.row_bias, epi.relu, pl.ksplit, pl.kb_per, part, counters, err_word);
 }
 
 // The matmul on prepared planes with CTA pairs (256-row tiles), per `pl`.
