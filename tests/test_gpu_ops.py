@@ -410,3 +410,34 @@ def test_reference_c_example_runs(gpu):
     assert r.returncode == 0, r.stderr
     assert "Lightning Core C API example: OK" in r.stdout
     assert "backend=cuda" in r.stdout and "cuda=1" in r.stdout
+
+
+@pytest.mark.parametrize("units,s,d,causal,post", [(37, 1000, 64, 1, 0), (37, 1000, 64, 1, 1), (300, 256, 128, 1, 1),
+                                                   (5, 333, 128, 0, 0), (128, 2048, 128, 1, 0)])
+def test_attention_bf16_persistent_matches_one_cta_per_tile(gpu, units, s, d, causal, post):
+    """The persistent one-tile kernel (tcgen05_1qp) runs the same per-tile arithmetic as the
+    one-CTA-per-tile kernel (tcgen05_1q), so their outputs agree bit for bit -- with the
+    postprocess, at head_dim 64 and 128, and with many Q tiles per resident CTA."""
+    import torch
+
+    torch.manual_seed(units * 7 + s)
+    q, k, v = (torch.randn((units, s, d), device="cuda").to(torch.bfloat16) for _ in range(3))
+    pol = gpu.default_attention_policy()
+    pol.upload_q = pol.upload_k = pol.upload_v = pol.upload_target = 0
+    pol.download_out = pol.download_v = 0
+    if post:
+        pol.output_scale, pol.output_bias, pol.output_relu = 0.5, -0.25, 1
+    outs = {}
+    for kern in ("tcgen05_1q", "tcgen05_1qp"):
+        o = torch.full_like(q, float("nan"))
+        gpu.tune_cache_set(gpu.TUNE_ATTENTION, s, d, causal, kern, gpu.BF16)
+        try:
+            gpu.check(gpu.lib.lcAttentionForward(C.c_void_p(q.data_ptr()), C.c_void_p(k.data_ptr()),
+                                                 C.c_void_p(v.data_ptr()), C.c_void_p(o.data_ptr()), units, s, d,
+                                                 causal, gpu.BF16, C.byref(pol), None))
+            torch.cuda.synchronize()
+        finally:
+            gpu.tune_cache_reset(gpu.TUNE_ATTENTION)
+        outs[kern] = o
+    assert torch.equal(outs["tcgen05_1q"], outs["tcgen05_1qp"])
+    assert bool(torch.isfinite(outs["tcgen05_1qp"].float()).all())
