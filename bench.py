@@ -659,6 +659,17 @@ def extra_configs(args, lc, torch, dev, sp):
                                                 "timing": "median of 5, L2 flushed before each"}
         del a, b, c
     del flush
+    # Attention train step (forward + MSE loss + dV + SGD on V), fp32, 16 heads [1024, 64]:
+    # forward 4*S^2*D plus dV = P^T dO 2*S^2*D per head (the P recomputation is not counted).
+    g.manual_seed(6)
+    tu, ts_, td = 16, 1024, 64
+    tq, tk, tv, tt = (torch.randn((tu, ts_, td), generator=g, device=dev) for _ in range(4))
+    to = torch.empty_like(tq)
+    ms = timeit(lambda: lc.check(L.lcAttentionTrainStep(ptr(tq), ptr(tk), ptr(tv), ptr(tt), ptr(to), C.c_float(1e-3),
+                                                        tu, ts_, td, 0, None, None, sp)), 10)
+    tfl = 6.0 * ts_ * ts_ * td * tu / (ms * 1e-3) / 1e12
+    res["train_step_f32_16x1024x64"] = {"ms": ms, "tflops": tfl, "frac_fp32_simt_nominal": tfl / 74.4}
+    del tq, tk, tv, tt, to
     rows, cols = 65536, 1024
     x = torch.randn((rows, cols), device=dev)
     y = torch.empty_like(x)
