@@ -48,12 +48,13 @@ void* tensor_map_encoder();
 namespace {
 
 constexpr int TILE = 128;               // query rows per CTA (= TMEM lanes)
-constexpr int TK = 64;                  // keys per KV tile
 constexpr int CHUNK_BYTES = 128 * 128;  // one [128 rows x 64 bf16] swizzled box = 16 KB
-constexpr int KCHUNK_BYTES = TK * 128;  // one [64 rows x 64 bf16] swizzled box = 8 KB
-constexpr int K_STAGES = 2;  // K_{j+2} loads as soon as S_j is done
-constexpr int V_STAGES = 2;  // V_{j+2} loads once PV_j is done (a separate producer thread)
-constexpr int P_BUFS = 2;    // P_j aliases TMEM score buffer j%2
+// KV tiles of TKV keys.  The TMEM score buffers take 128 columns whatever TKV is, so there are
+// NB = 128 / TKV of them; the K and V rings have NB stages; P_j aliases score buffer j % NB, and
+// S_{j+NB} can only be issued once P.V_j has read P_j.  The library launches TKV = 64; 32-key
+// tiles (four buffers, three S tiles in flight) were exact but 23% slower at config 3 (0.186
+// against 0.152 ms): the per-tile softmax costs, not the S -> P.V chain, then dominate.
+constexpr int kMaxBufs = 4;
 constexpr int NUM_THREADS = 224;  // 7 warps: K/Q loader, MMA, 4 softmax, V loader
 constexpr uint32_t TMEM_COLS = 256;  // S buffers at 0 and 64, O at 128: two CTAs fit one SM
 constexpr float LOG2E = 1.4426950408889634f;
@@ -67,11 +68,11 @@ constexpr int kUnitGroup = 16;
 
 struct AttnTail {
   uint64_t q_full;
-  uint64_t k_full[K_STAGES];
-  uint64_t v_full[V_STAGES];
-  uint64_t s_full[2];
-  uint64_t p_full[2];       // p_full[b]: P_j with j%2 == b is in TMEM (4 warp arrivals)
-  uint64_t o_done[P_BUFS];  // o_done[b] completes for PV_j with j%2 == b (one phase per 2 tiles)
+  uint64_t k_full[kMaxBufs];
+  uint64_t v_full[kMaxBufs];
+  uint64_t s_full[kMaxBufs];  // s_full[b]: S_j with j%NB == b is in TMEM (one commit)
+  uint64_t p_full[kMaxBufs];  // p_full[b]: P_j with j%NB == b is in TMEM (4 warp arrivals)
+  uint64_t o_done[kMaxBufs];  // o_done[b] completes for PV_j with j%NB == b (one phase per NB tiles)
   uint64_t drain;
   uint64_t o_staged;  // the 4 softmax warps have written the bf16 O tile into the Q buffer
   uint64_t item_full[4];   // persistent form: item ring published by the Q/K producer thread
@@ -81,17 +82,20 @@ struct AttnTail {
   int abort_flag;
 };
 
-template <int D>
+template <int D, int TKV>
 struct Layout {
+  static constexpr int NB = 128 / TKV;                    // score buffers = K/V ring stages
   static constexpr int NCH = D / 64;                      // 64-column chunks per row
+  static constexpr int KCH = TKV * 128;                   // one [TKV rows x 64 bf16] swizzled box
   static constexpr int Q_BYTES = NCH * CHUNK_BYTES;
-  static constexpr int KV_BYTES = NCH * KCHUNK_BYTES;
+  static constexpr int KV_BYTES = NCH * KCH;
   static constexpr int Q_OFF = 0;
   static constexpr int K_OFF = Q_OFF + Q_BYTES;
-  static constexpr int V_OFF = K_OFF + K_STAGES * KV_BYTES;
-  static constexpr int TAIL_OFF = V_OFF + V_STAGES * KV_BYTES;
-  // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel without static shared memory starts
-  // 1 KB-aligned; the kernel checks this and bails out with an error code otherwise.
+  static constexpr int V_OFF = K_OFF + NB * KV_BYTES;
+  static constexpr int TAIL_OFF = V_OFF + NB * KV_BYTES;
+  // No alignment slack: two CTAs must fit one SM's 228 KB.  The dynamic window of a kernel
+  // without static shared memory starts 1 KB-aligned; the kernel checks this and bails out
+  // with an error code otherwise.
   static constexpr size_t SMEM = TAIL_OFF + sizeof(AttnTail);
 };
 
@@ -179,9 +183,10 @@ __device__ __forceinline__ void fa_item(const FaParams& p, int b, int& qt, int& 
   qt = p.nq - 1 - r / gu;
   unit = g * p.group + r % gu;
 }
+template <int TKV>
 __device__ __forceinline__ int fa_kv_tiles(const FaParams& p, int qt) {
-  const int kv_tiles_all = (p.seq + TK - 1) / TK;
-  return p.causal ? min(kv_tiles_all, (qt * TILE + TILE - 1) / TK + 1) : kv_tiles_all;
+  const int kv_tiles_all = (p.seq + TKV - 1) / TKV;
+  return p.causal ? min(kv_tiles_all, (qt * TILE + TILE - 1) / TKV + 1) : kv_tiles_all;
 }
 
 // The CTA's it-th item: blockIdx.x alone without PERSIST; otherwise read from the item ring
@@ -214,12 +219,15 @@ __device__ __forceinline__ bool fa_take_item(AttnTail* st, int it, int b0, int n
 // previous item's last S MMA is done, and O is written from registers, so the Q buffer is never
 // needed for the epilogue.  This removes the per-CTA launch gap, set-up and cold Q wait, which
 // the co-resident CTA had mostly hidden already: measured no faster at config 3.
-template <int D, bool PERSIST>
+template <int D, bool PERSIST, int TKV>
 __global__ void __launch_bounds__(NUM_THREADS, 2)
     fa_fwd_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                   const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                   const FaParams p) {
-  using LY = Layout<D>;
+  using LY = Layout<D, TKV>;
+  constexpr int NB = LY::NB;
+  constexpr int TK = TKV;
+  constexpr int KCHUNK_BYTES = LY::KCH;
   constexpr int NCH = LY::NCH;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if ((smem_u32(smem_raw) & 1023u) != 0) {  // the 128-byte swizzle atoms need 1 KB alignment
@@ -239,14 +247,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
 
   if (threadIdx.x == 0) {
     mbar_init(&st->q_full, 1);
-    for (int s = 0; s < K_STAGES; ++s) mbar_init(&st->k_full[s], 1);
-    for (int s = 0; s < V_STAGES; ++s) mbar_init(&st->v_full[s], 1);
-    mbar_init(&st->s_full[0], 1);
-    mbar_init(&st->s_full[1], 1);
-    mbar_init(&st->p_full[0], 4);
-    mbar_init(&st->p_full[1], 4);
-    mbar_init(&st->o_done[0], 1);
-    mbar_init(&st->o_done[1], 1);
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(&st->k_full[s], 1);
+      mbar_init(&st->v_full[s], 1);
+      mbar_init(&st->s_full[s], 1);
+      mbar_init(&st->p_full[s], 4);
+      mbar_init(&st->o_done[s], 1);
+    }
     mbar_init(&st->drain, 1);
     mbar_init(&st->o_staged, 4);
     for (int r = 0; r < kItemSlots; ++r) {
@@ -307,10 +314,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         if (b >= n_items) break;
         int qt, unit;
         fa_item(p, b, qt, unit);
-        const int n_kv = fa_kv_tiles(p, qt);
+        const int n_kv = fa_kv_tiles<TKV>(p, qt);
         int nxt = n_items;
         for (int j = 0; j < n_kv; ++j) {
-          const int ks = g % K_STAGES;
+          const int ks = g % NB;
           // The next item is claimed a few KV steps before this item ends: late enough that claims
           // follow the order CTAs run dry in (greedy balance), early enough that the atomic's
           // latency is hidden.
@@ -328,12 +335,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
               tma_prefetch_l2_3d(&map_v, c * 64, TK, nunit);
             }
           }
-          if (j + K_STAGES < n_kv)  // warm L2 for the K tile that will take this slot next
-            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + K_STAGES) * TK, unit);
+          if (j + NB < n_kv)  // warm L2 for the K tile that will take this slot next
+            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_k, c * 64, (j + NB) * TK, unit);
           // Slot ks last held the K of global step g-2: that S MMA must have finished reading it.
           // Every MMA group has exactly one commit (S_g -> s_full[g&1]), and this thread observes
           // S_0, S_1, ... in order, so each parity wait is unambiguous.
-          if (g >= K_STAGES && !mbar_wait_bounded(&st->s_full[(g - K_STAGES) & 1], ((g - K_STAGES) >> 1) & 1,
+          if (g >= NB && !mbar_wait_bounded(&st->s_full[(g - NB) % NB], ((g - NB) / NB) & 1,
                                                   abort_flag, p.err_word, kErrAttnLoadWait)) {
             ok = false;
             break;
@@ -345,7 +352,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
             // This item's Q replaces the previous one once the previous item's last S MMA (global
             // step g-2 now) is done; the next completion of that barrier needs this Q, so the
             // parity wait is unambiguous.
-            if (!mbar_wait_bounded(&st->s_full[(g - 2) & 1], ((g - 2) >> 1) & 1, abort_flag, p.err_word,
+            if (!mbar_wait_bounded(&st->s_full[(g - 2) % NB], ((g - 2) / NB) & 1, abort_flag, p.err_word,
                                    kErrAttnLoadWait)) {
               ok = false;
               break;
@@ -360,7 +367,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       }
       if (!ok) {
         drain(&st->q_full, (q_loads - 1) & 1);
-        for (int x = g > K_STAGES ? g - K_STAGES : 0; x < g; ++x) drain(&st->k_full[x % K_STAGES], (x / K_STAGES) & 1);
+        for (int x = g > NB ? g - NB : 0; x < g; ++x) drain(&st->k_full[x % NB], (x / NB) & 1);
       }
     }
   } else if (warp == 6) {
@@ -378,14 +385,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         if (b < 0) break;
         int qt, unit;
         fa_item(p, b, qt, unit);
-        const int n_kv = fa_kv_tiles(p, qt);
+        const int n_kv = fa_kv_tiles<TKV>(p, qt);
         for (int j = 0; j < n_kv; ++j) {
-          const int vs = g % V_STAGES;
-          if (j + V_STAGES < n_kv)
-            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + V_STAGES) * TK, unit);
+          const int vs = g % NB;
+          if (j + NB < n_kv)
+            for (int c = 0; c < NCH; ++c) tma_prefetch_l2_3d(&map_v, c * 64, (j + NB) * TK, unit);
           // Slot vs last held the V of step g-2: that PV (one commit: o_done[g%2]) must be done.
           // PV_g cannot complete before V_g is issued here, so the parity wait is unambiguous.
-          if (g >= V_STAGES && !mbar_wait_bounded(&st->o_done[(g - V_STAGES) % P_BUFS], ((g - V_STAGES) >> 1) & 1,
+          if (g >= NB && !mbar_wait_bounded(&st->o_done[(g - NB) % NB], ((g - NB) / NB) & 1,
                                                   abort_flag, p.err_word, kErrAttnLoadWait)) {
             ok = false;
             break;
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
       }
       if (!ok)
-        for (int x = g > V_STAGES ? g - V_STAGES : 0; x < g; ++x) drain(&st->v_full[x % V_STAGES], (x / V_STAGES) & 1);
+        for (int x = g > NB ? g - NB : 0; x < g; ++x) drain(&st->v_full[x % NB], (x / NB) & 1);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -407,13 +414,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const uint32_t q_addr = smem_u32(sQ);
     bool ok = true, issued = false;
     auto issue_s = [&](int gs) -> bool {  // S of global step gs into TMEM buffer gs&1
-      const int s = gs % K_STAGES;
-      if (!warp_wait_poll(&st->k_full[s], (gs / K_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
+      const int s = gs % NB;
+      if (!warp_wait_poll(&st->k_full[s], (gs / NB) & 1, abort_flag, p.err_word, kErrAttnMmaWait))
         return false;
       tc_fence_after();
       const uint64_t qd = smem_desc_sw128(q_addr, 16, 1024);
       const uint64_t kd = smem_desc_sw128(smem_u32(sK + s * LY::KV_BYTES), 16, 1024);
-      const uint32_t d_tmem = tmem + static_cast<uint32_t>((gs & 1) * TK);
+      const uint32_t d_tmem = tmem + static_cast<uint32_t>((gs % NB) * TK);
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t qo16 = ((kk >> 2) * CHUNK_BYTES + (kk & 3) * 32) >> 4;  // address field: bytes / 16
@@ -421,7 +428,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         umma_f16_ss_w(d_tmem, qd + qo16, kd + ko16, IDESC_S, kk > 0 ? 1u : 0u);
       }
       issued = true;
-      umma_commit_w(&st->s_full[gs & 1]);  // the only commit of this MMA group
+      umma_commit_w(&st->s_full[gs % NB]);  // the only commit of this MMA group
       return true;
     };
     int g = 0;  // global KV step of the item's first tile
@@ -434,36 +441,39 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       if (b < 0) break;
       int qt, unit;
       fa_item(p, b, qt, unit);
-      const int n_kv = fa_kv_tiles(p, qt);
+      const int n_kv = fa_kv_tiles<TKV>(p, qt);
       // q_full completes once per item; the next Q needs this item's last S, so parity it&1 is unambiguous.
-      ok = warp_wait_poll(&st->q_full, it & 1, abort_flag, p.err_word, kErrAttnMmaWait) && issue_s(g);
+      ok = warp_wait_poll(&st->q_full, it & 1, abort_flag, p.err_word, kErrAttnMmaWait);
+      // S runs NB-1 tiles ahead of P.V: S_{j+NB-1} goes into the buffer of P_{j-1}, which
+      // P.V_{j-1} (issued before it, executed in order) has read.
+      for (int j = 0; j < NB - 1 && j < n_kv && ok; ++j) ok = issue_s(g + j);
       for (int j = 0; j < n_kv && ok; ++j) {
         const int gg = g + j;
-        const int s = gg % V_STAGES;
-        if (j + 1 < n_kv && !issue_s(gg + 1)) {
+        const int s = gg % NB;
+        if (j + NB - 1 < n_kv && !issue_s(gg + NB - 1)) {
           ok = false;
           break;
         }
-        // One barrier per TMEM buffer: p_full[gg&1] next completes for P_{gg+2}, which needs
-        // S_{gg+2}, issued only after this wait, so the parity wait is unambiguous.
-        if (!warp_wait_poll(&st->p_full[gg & 1], (gg >> 1) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
-            !warp_wait_poll(&st->v_full[s], (gg / V_STAGES) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
+        // One barrier per TMEM buffer: p_full[gg%NB] next completes for P_{gg+NB}, which needs
+        // S_{gg+NB}, issued only after this wait, so the parity wait is unambiguous.
+        if (!warp_wait_poll(&st->p_full[gg % NB], (gg / NB) & 1, abort_flag, p.err_word, kErrAttnMmaWait) ||
+            !warp_wait_poll(&st->v_full[s], (gg / NB) & 1, abort_flag, p.err_word, kErrAttnMmaWait)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint64_t vd = smem_desc_sw128(smem_u32(sV + s * LY::KV_BYTES), KCHUNK_BYTES, 1024);
-        const uint32_t o_tmem = tmem + 2 * TK;
+        const uint32_t o_tmem = tmem + NB * TK;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk) {
           // A = P in TMEM (lanes = rows, 2 keys per column): +8 columns per 16 keys.  B = V,
           // MN-major: 64-column d chunks 8 KB apart (LBO), +16 key rows * 128 B per step.  The
           // item's first PV overwrites O, which the softmax warps read out (previous item's
           // epilogue) before they hand over this item's first P.
-          const uint32_t a_tmem = tmem + static_cast<uint32_t>((gg % P_BUFS) * TK + kk * 8);
+          const uint32_t a_tmem = tmem + static_cast<uint32_t>((gg % NB) * TK + kk * 8);
           umma_f16_ts_w(o_tmem, a_tmem, vd + (kk * 2048 >> 4), IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit_w(&st->o_done[gg % P_BUFS]);  // the only commit of this MMA group
+        umma_commit_w(&st->o_done[gg % NB]);  // the only commit of this MMA group
       }
       g += n_kv;
     }
@@ -478,7 +488,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // row within the Q tile == TMEM lane
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t o_tmem = tmem + lane_base + 2 * TK;
+    const uint32_t o_tmem = tmem + lane_base + NB * TK;
     bool ok = true;
     int g = 0;        // global KV step of the item's first tile
     for (int it = 0; ok; ++it) {
@@ -490,13 +500,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
       if (b < 0) break;
       int qt, unit;
       fa_item(p, b, qt, unit);
-      const int n_kv = fa_kv_tiles(p, qt);
+      const int n_kv = fa_kv_tiles<TKV>(p, qt);
       const int q0 = qt * TILE;
       const int qrow = q0 + row;
       float m = -INFINITY, l = 0.0f;
       for (int j = 0; j < n_kv; ++j) {
         const int gg = g + j;
-        if (!warp_wait_poll(&st->s_full[gg & 1], (gg >> 1) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
+        if (!warp_wait_poll(&st->s_full[gg % NB], (gg / NB) & 1, abort_flag, p.err_word, kErrAttnSoftmaxWait)) {
           ok = false;
           break;
         }
@@ -504,7 +514,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         // Both 32-column score loads in flight before a single wait.
         uint32_t r[TK / 32][32];
         {
-          const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((gg & 1) * TK);
+          const uint32_t s_tmem = tmem + lane_base + static_cast<uint32_t>((gg % NB) * TK);
 #pragma unroll
           for (int c = 0; c < TK / 32; ++c) tmem_ld32(s_tmem + c * 32, r[c]);
           tmem_wait_ld();
@@ -539,7 +549,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         }
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           // O is rescaled in place: PV_{gg-1} must have landed first.
-          if (!warp_wait_poll(&st->o_done[(gg - 1) % P_BUFS], ((gg - 1) >> 1) & 1, abort_flag, p.err_word,
+          if (!warp_wait_poll(&st->o_done[(gg - 1) % NB], ((gg - 1) / NB) & 1, abort_flag, p.err_word,
                               kErrAttnCorrectionWait)) {
             ok = false;
             break;
@@ -560,7 +570,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         // visible, so the first tile sets it).  Packed partial sums keep the adds independent.
         const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m, -m);
         uint64_t ps2[4] = {0, 0, 0, 0};
-        const uint32_t p_tmem = tmem + lane_base + static_cast<uint32_t>((gg & 1) * TK);
+        const uint32_t p_tmem = tmem + lane_base + static_cast<uint32_t>((gg % NB) * TK);
 #pragma unroll
         for (int gq = 0; gq < TK / 32; ++gq) {
           uint32_t w[16];
@@ -589,17 +599,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 2)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&st->p_full[gg & 1]);
+        if (lane == 0) mbar_arrive(&st->p_full[gg % NB]);
       }
       if (!ok) break;
       // The last two PVs (one per P buffer) must have landed in O.  The next completion of either
       // barrier needs a P of the next item, which these warps have not handed over yet.
       const int gl = g + n_kv - 1;
       if (n_kv >= 2)
-        ok = warp_wait_poll(&st->o_done[(gl - 1) % P_BUFS], ((gl - 1) >> 1) & 1, abort_flag, p.err_word,
+        ok = warp_wait_poll(&st->o_done[(gl - 1) % NB], ((gl - 1) / NB) & 1, abort_flag, p.err_word,
                             kErrAttnCorrectionWait);
       if (ok)
-        ok = warp_wait_poll(&st->o_done[gl % P_BUFS], (gl >> 1) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait);
+        ok = warp_wait_poll(&st->o_done[gl % NB], (gl / NB) & 1, abort_flag, p.err_word, kErrAttnCorrectionWait);
       if (!ok) break;
       tc_fence_after();
       const float inv = 1.0f / l;
@@ -1142,20 +1152,20 @@ cudaError_t launch_fa2q(const AttnArgs& a, cudaStream_t s) {
 }
 
 
-template <int D, bool PERSIST>
+template <int D, bool PERSIST, int TKV = 64>
 cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   DeviceCtx* ctx = device_ctx();
   if (!ctx) return cudaErrorNoDevice;
   CUtensorMap mq, mk, mv, mo;
-  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D, TILE) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D, TK) ||
-      !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TK) || !make_tmap_heads(&mo, a.out, a.units, a.seq, D, TILE))
+  if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D, TILE) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D, TKV) ||
+      !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TKV) || !make_tmap_heads(&mo, a.out, a.units, a.seq, D, TILE))
     return cudaErrorInvalidValue;
   static bool attr_set = false;  // benign race: idempotent
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(Layout<D>::SMEM));
+    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(Layout<D, TKV>::SMEM));
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
@@ -1177,7 +1187,7 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   if (items > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
   // Persistent form: two resident CTAs per SM.
   const long long blocks = PERSIST ? std::min<long long>(items, 2LL * std::max(ctx->sm_count, 1)) : items;
-  fa_fwd_kernel<D, PERSIST><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D>::SMEM, s>>>(
+  fa_fwd_kernel<D, PERSIST, TKV><<<static_cast<unsigned>(blocks), NUM_THREADS, Layout<D, TKV>::SMEM, s>>>(
       mq, mk, mv, mo, p);
   return cudaGetLastError();
 }
