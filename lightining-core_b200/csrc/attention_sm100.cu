@@ -63,7 +63,8 @@ constexpr float RESCALE_THRESHOLD = 8.0f;
 // all its units come first.  Heavy-first inside a group shortens the causal tail (light tiles run
 // last); a group small enough to keep its units' K/V in L2 keeps DRAM reads at the algorithmic
 // bytes.  Config 3 causal, one-tile kernel: 0.162 ms with one unit per group, 0.150-0.152 ms with
-// 16 (256 CTAs per group), 0.156 ms with 128.
+// 16 (256 CTAs per group), 0.156 ms with 128; a later sweep on one box gave 4: 0.162, 8: 0.158,
+// 12: 0.164, 16: 0.154, 24: 0.166, 32: 0.154, 64: 0.154 ms.
 constexpr int kUnitGroup = 16;
 
 struct AttnTail {
