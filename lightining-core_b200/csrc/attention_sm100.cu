@@ -1125,12 +1125,15 @@ cudaError_t launch_fa2q(const AttnArgs& a, cudaStream_t s) {
   if (!make_tmap_heads(&mq, a.q, a.units, a.seq, q2::D, 128) || !make_tmap_heads(&mk, a.k, a.units, a.seq, q2::D, 128) ||
       !make_tmap_heads(&mv, a.v, a.units, a.seq, q2::D, 128) || !make_tmap_heads(&mo, a.out, a.units, a.seq, q2::D, 128))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fa2q_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(q2::SMEM));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(fa2q_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(q2::SMEM));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   FaParams p;
   p.sched = nullptr;
@@ -1161,14 +1164,17 @@ cudaError_t launch_fa(const AttnArgs& a, cudaStream_t s) {
   if (!make_tmap_heads(&mq, a.q, a.units, a.seq, D, TILE) || !make_tmap_heads(&mk, a.k, a.units, a.seq, D, TKV) ||
       !make_tmap_heads(&mv, a.v, a.units, a.seq, D, TKV) || !make_tmap_heads(&mo, a.out, a.units, a.seq, D, TILE))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(Layout<D, TKV>::SMEM));
-    if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(Layout<D, TKV>::SMEM));
+      if (e != cudaSuccess) return e;
+      e = cudaFuncSetAttribute(fa_fwd_kernel<D, PERSIST, TKV>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   FaParams p;
   p.out = static_cast<__nv_bfloat16*>(a.out);

@@ -642,12 +642,15 @@ cudaError_t attention_f32_tc_planes(const AttnArgs& a, float* ws, size_t nqk, si
       !make_tmap_f32_3d(&mkh, kh, a.units, a.seq, D, TK) || !make_tmap_f32_3d(&mkl, kl, a.units, a.seq, D, TK) ||
       !make_tmap_f32_3d(&mvh, vh, a.units, D, sp, D) || !make_tmap_f32_3d(&mvl, vl, a.units, D, sp, D))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent
-  if (!attr_set) {
-    if ((e = cudaFuncSetAttribute(fa_f32_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(SMEM_BYTES))) != cudaSuccess)
-      return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      if ((e = cudaFuncSetAttribute(fa_f32_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(SMEM_BYTES))) != cudaSuccess)
+        return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   // One pre-pass launch: Q and K row splits (unless the caller wrote those planes) and V^T tiles.
   const int nrb = qk_ready ? 0

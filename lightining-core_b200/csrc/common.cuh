@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #ifndef LC_WAIT_TIMEOUT_NS
@@ -45,6 +46,22 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+
+// Function attributes (the dynamic shared-memory limit, the carveout) belong to a device's
+// context, so a process that drives several GPUs sets them once per device: `done` holds one bit
+// per device ordinal whose attributes are set.  set() is idempotent, so threads that race on one
+// device and both run it are harmless.
+template <class Set>
+inline cudaError_t once_per_device(std::atomic<unsigned long long>& done, Set set) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = set();
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
 
 // Error-word codes (low byte = site, upper bits = kernel id).
 enum : unsigned {

@@ -737,15 +737,16 @@ cudaError_t conv_implicit_run(const float* x, const float* w, const float* bias,
       e = cudaErrorInvalidValue;
   }
   if (e == cudaSuccess) {
-    static bool attr_set = false;  // benign race: idempotent attribute set (largest size once)
-    if (!attr_set) {
-      e = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(conv_im2col_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    // The largest size each kernel can take, once per device.
+    static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+    e = once_per_device(attr_done, []() -> cudaError_t {
+      cudaError_t r = cudaFuncSetAttribute(conv_implicit_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(1024 + STAGES * STAGE_MAX + sizeof(Tail)));
+      if (r == cudaSuccess)
+        r = cudaFuncSetAttribute(conv_im2col_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(pairk::SMEM_LIMIT));
-      if (e == cudaSuccess) attr_set = true;
-    }
+      return r;
+    });
   }
   if (e == cudaSuccess) {
     ConvParams p;

@@ -588,12 +588,15 @@ cudaError_t gemm_bf16_tc(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bf
   if (!make_tmap_bf16_2d(&ma, a, m, k, k, BM, BK)) return cudaErrorInvalidValue;
   if (!make_tmap_bf16_2d(&mb, b, k, n, n, BK, 64)) return cudaErrorInvalidValue;
   if (!make_tmap_bf16_2d(&mc, c, m, n, n, 32, 64)) return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent attribute set
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(SMEM_BYTES));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + BN - 1) / BN);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
@@ -612,12 +615,15 @@ cudaError_t gemm_bf16_tc2(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_b
   if (!make_tmap_bf16_2d(&ma, a, m, k, k, pair::BM, pair::BK)) return cudaErrorInvalidValue;
   if (!make_tmap_bf16_2d(&mb, b, k, n, n, pair::BK, 64)) return cudaErrorInvalidValue;
   if (!make_tmap_bf16_2d(&mc, c, m, n, n, 32, 64)) return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent attribute set
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(pair::gemm_bf16_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(pair::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(pair::gemm_bf16_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(pair::SMEM_BYTES));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   const int tiles = ((m + pair::TILE_M - 1) / pair::TILE_M) * ((n + pair::BN - 1) / pair::BN);
   const int clusters = tiles < ctx->sm_count / 2 ? tiles : ctx->sm_count / 2;

@@ -834,15 +834,18 @@ cudaError_t launch_planes(DeviceCtx* ctx, const float* a_hi, const float* a_lo, 
   if (!make_tmap_f32_2d(&mah, a_hi, m, kp, BM, BK) || !make_tmap_f32_2d(&mal, a_lo, m, kp, BM, BK) ||
       !make_tmap_f32_2d(&mbh, b_hi, n, kp, bn, BK) || !make_tmap_f32_2d(&mbl, b_lo, n, kp, bn, BK))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;  // benign race: idempotent attribute set
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes_for(128)));
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gemm_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(smem_bytes_for(64)));
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem_bytes_for(128)));
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(gemm_tf32x3_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem_bytes_for(64)));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   const int tiles = ((m + BM - 1) / BM) * ((n + bn - 1) / bn);
   const int grid = tiles < ctx->sm_count ? tiles : ctx->sm_count;
@@ -885,12 +888,15 @@ template <int BN>
 cudaError_t launch_pair_bn(const CUtensorMap& mah, const CUtensorMap& mal, const CUtensorMap& pbh,
                            const CUtensorMap& pbl, int m, int n, int kp, const Epi& epi, const PairPlan& pl,
                            float* part, unsigned* counters, unsigned* err_word, int clusters_max, cudaStream_t s) {
-  static bool attr = false;  // benign race: idempotent attribute set
-  if (!attr) {
-    const cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(pairg::smem_bytes<BN>()));
-    if (e != cudaSuccess) return e;
-    attr = true;
+  static std::atomic<unsigned long long> attr_done{0};  // devices with the attributes set
+  {
+    const cudaError_t ea = once_per_device(attr_done, [&]() -> cudaError_t {
+      const cudaError_t e = cudaFuncSetAttribute(gemm_tf32x3_pair_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(pairg::smem_bytes<BN>()));
+      if (e != cudaSuccess) return e;
+      return cudaSuccess;
+    });
+    if (ea != cudaSuccess) return ea;
   }
   const int items = pl.tiles * pl.ksplit;
   const int clusters = items < clusters_max ? items : clusters_max;
