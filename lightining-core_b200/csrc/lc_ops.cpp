@@ -18,31 +18,52 @@ namespace lcb {
 namespace {
 
 // Per-thread, per-device staging buffers for host-pointer (upload/download) calls; they grow
-// by 1.5x like the reference's Metal buffers (src/attention_metal.mm:1082) and are reused.
+// by 1.5x like the reference's Metal buffers (src/attention_metal.mm:1082) and are reused.  A call
+// that returns before its work is done (no synchronize, no download) may leave a slot in use on
+// its stream; each slot therefore carries an event recorded after the last call that used it, and
+// a later call on another stream waits for that event before touching the slot (calls on the
+// same stream are ordered by the stream itself).
 struct Staging {
   struct Slot {
     void* ptr = nullptr;
     size_t bytes = 0;
+    cudaEvent_t done = nullptr;   // recorded on `stream` after the last call that used the slot
+    cudaStream_t stream = nullptr;
   };
   std::vector<Slot> slots[64];
   ~Staging() {
     // Buffers are released with the thread; contexts may already be gone at process exit.
   }
-  cudaError_t get(int dev, int slot, size_t bytes, void** out) {
+  cudaError_t get(int dev, int slot, size_t bytes, cudaStream_t s, void** out) {
     auto& v = slots[dev];
     if (static_cast<int>(v.size()) <= slot) v.resize(slot + 1);
-    Slot& s = v[slot];
-    if (s.bytes < bytes) {
-      if (s.ptr) cudaFree(s.ptr);
-      s.ptr = nullptr;
-      s.bytes = 0;
+    Slot& sl = v[slot];
+    if (sl.bytes < bytes) {
+      if (sl.ptr) cudaFree(sl.ptr);  // synchronizes the device: no earlier use is still running
+      sl.ptr = nullptr;
+      sl.bytes = 0;
       const size_t want = bytes + bytes / 2;
-      cudaError_t e = device_malloc(&s.ptr, want);
+      cudaError_t e = device_malloc(&sl.ptr, want);
       if (e != cudaSuccess) return e;
-      s.bytes = want;
+      sl.bytes = want;
+    } else if (sl.done && sl.stream != s) {
+      cudaError_t e = cudaStreamWaitEvent(s, sl.done, 0);
+      if (e != cudaSuccess) return e;
     }
-    *out = s.ptr;
+    *out = sl.ptr;
     return cudaSuccess;
+  }
+  // After a call: slots [0, n) of device `dev` were used by work enqueued on stream s.
+  void release(int dev, int n, cudaStream_t s) {
+    auto& v = slots[dev];
+    for (int i = 0; i < n && i < static_cast<int>(v.size()); ++i) {
+      Slot& sl = v[i];
+      if (!sl.done && cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming) != cudaSuccess) {
+        sl.done = nullptr;
+        continue;
+      }
+      if (cudaEventRecord(sl.done, s) == cudaSuccess) sl.stream = s;
+    }
   }
 };
 thread_local Staging t_staging;
@@ -51,6 +72,11 @@ thread_local Staging t_staging;
 class Io {
  public:
   explicit Io(cudaStream_t s) : s_(s) { cudaGetDevice(&dev_); }
+  ~Io() {
+    if (slot_ > 0) t_staging.release(dev_, slot_, s_);
+  }
+  Io(const Io&) = delete;
+  Io& operator=(const Io&) = delete;
   // Input: host pointer -> copied into staging slot; device pointer -> used directly.
   cudaError_t in(const void* p, size_t bytes, bool host, const void** dev) {
     if (!host) {
@@ -58,7 +84,7 @@ class Io {
       return cudaSuccess;
     }
     void* d = nullptr;
-    cudaError_t e = t_staging.get(dev_, slot_++, bytes, &d);
+    cudaError_t e = t_staging.get(dev_, slot_++, bytes, s_, &d);
     if (e != cudaSuccess) return e;
     e = cudaMemcpyAsync(d, p, bytes, cudaMemcpyHostToDevice, s_);
     *dev = d;
@@ -70,9 +96,9 @@ class Io {
       *dev = p;
       return cudaSuccess;
     }
-    return t_staging.get(dev_, slot_++, bytes, dev);
+    return t_staging.get(dev_, slot_++, bytes, s_, dev);
   }
-  cudaError_t scratch(size_t bytes, void** dev) { return t_staging.get(dev_, slot_++, bytes, dev); }
+  cudaError_t scratch(size_t bytes, void** dev) { return t_staging.get(dev_, slot_++, bytes, s_, dev); }
   cudaError_t finish(void* host_out, const void* dev_out, size_t bytes, bool download, bool sync) {
     cudaError_t e = cudaSuccess;
     if (download) e = cudaMemcpyAsync(host_out, dev_out, bytes, cudaMemcpyDeviceToHost, s_);

@@ -152,3 +152,41 @@ def test_fp32_tensor_core_calls_overlap_across_streams(gpu):
     for i in range(2):
         q, k, v = (t.cpu().numpy() for t in qs[3 * i:3 * i + 3])
         close_enough(P.attention(q[0], k[0], v[0]), outs[i][0].cpu().numpy(), 1e-4, 1e-4)
+
+
+def test_async_host_input_calls_on_two_streams_keep_their_inputs(gpu):
+    """Two asynchronous calls with host inputs (upload set, no download, no synchronize) on two
+    streams from one thread: both go through this thread's staging buffers, so the second call's
+    uploads must wait until the first call's kernel has read them.  Each output must equal the
+    output of the same call made alone and synchronously (same kernel, bit for bit)."""
+    import torch
+
+    L = gpu.lib
+    units, seq, d = 48, 2048, 128
+    g = torch.Generator().manual_seed(9)
+    host = [torch.randn((units, seq, d), generator=g).to(torch.bfloat16).pin_memory() for _ in range(6)]
+    outs = [torch.empty((units, seq, d), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    want = [torch.empty_like(outs[0]) for _ in range(2)]
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    pol = gpu.default_attention_policy()
+    pol.upload_q = pol.upload_k = pol.upload_v = 1
+    pol.download_out = 0
+    pol.synchronize = 0
+
+    def call(i, out, stream):
+        q, k, v = host[3 * i:3 * i + 3]
+        return L.lcAttentionForward(_p(q), _p(k), _p(v), _p(out), units, seq, d, 1, gpu.BF16, C.byref(pol),
+                                    C.c_void_p(stream.cuda_stream))
+
+    for i in range(2):  # alone, one at a time
+        assert call(i, want[i], streams[0]) == gpu.LC_SUCCESS
+        torch.cuda.synchronize()
+    for _ in range(3):  # back to back on two streams, nothing synchronised in between
+        for o in outs:
+            o.zero_()
+        torch.cuda.synchronize()
+        assert call(0, outs[0], streams[0]) == gpu.LC_SUCCESS
+        assert call(1, outs[1], streams[1]) == gpu.LC_SUCCESS
+        torch.cuda.synchronize()
+        for i in range(2):
+            assert torch.equal(outs[i], want[i]), i
