@@ -412,6 +412,25 @@ def test_reference_c_example_runs(gpu):
     assert "backend=cuda" in r.stdout and "cuda=1" in r.stdout
 
 
+def test_reference_cpp_ops_route_kcuda_here(gpu):
+    """The reference's own C++ operator templates (lightning_core::ops::vectorAdd, matMulWithPolicy
+    at 256^3 and 1024^3, matrixSubWithPolicy, matrixDivWithPolicy) called with Device::kCUDA, whose
+    hooks lightining-core_b200/integration/reference_cuda_hooks.cpp serves from liblc_b200.so:
+    each result matches the same call with Device::kCPU (the reference's CPU loops), and every
+    kCUDA call was completed by liblc_b200.so rather than by the reference's CPU fallback."""
+    import os
+    import subprocess
+
+    from conftest import ROOT
+
+    exe = os.path.join(ROOT, "oracle", "_ref", "reference_ops_on_cuda")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/reference_ops_on_cuda not built (needs the reference sources)")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "kCUDA calls 5, served by liblc_b200.so 5" in r.stdout, r.stdout
+
+
 @pytest.mark.parametrize("units,s,d,causal,post", [(37, 1000, 64, 1, 0), (37, 1000, 64, 1, 1), (300, 256, 128, 1, 1),
                                                    (5, 333, 128, 0, 0), (128, 2048, 128, 1, 0)])
 def test_attention_bf16_persistent_matches_one_cta_per_tile(gpu, units, s, d, causal, post):
