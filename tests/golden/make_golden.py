@@ -34,9 +34,34 @@ def bf16r(x):
     return O.port().bf16_round(np.ascontiguousarray(x, np.float32))
 
 
+REF_ROOT = os.environ.get("LC_REF_ROOT", os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(HERE))),
+                                                       "reference"))
+
+
+def readme_layer_norm():
+    """The reference's LN helper is Python inside its README's benchmark script
+    (README.md:2267-2270, `_layer_norm_np`, used at :3779-3818): the function's own lines are
+    taken from the README and executed as they stand, so the fixture comes from the reference's
+    code, not from a restatement."""
+    lines = open(os.path.join(REF_ROOT, "README.md"), encoding="utf-8").read().splitlines()
+    start = next(i for i, ln in enumerate(lines) if ln.startswith("def _layer_norm_np("))
+    end = start + 1
+    while end < len(lines) and (lines[end].startswith(("\t", " ")) or not lines[end].strip()):
+        end += 1
+    ns = {"np": np}
+    exec("\n".join(lines[start:end]), ns)  # noqa: S102 - the reference's own helper
+    return ns["_layer_norm_np"]
+
+
 def main():
     R = O.ref()
     out = {}
+    # LN helper: README shapes are [1024|2048, 1024] of np.random.rand; smaller row counts here.
+    ln = readme_layer_norm()
+    rng = np.random.default_rng(8)
+    for rows, cols in ((16, 1024), (5, 333)):
+        x = rng.random((rows, cols)).astype(np.float32)
+        out[f"ln_readme_{rows}x{cols}"] = dict(x=x, out=ln(x.copy()))
 
     # --- reference known-answer tests ----------------------------------------------------
     q = np.array([[1, 0], [0, 1]], np.float32)

@@ -347,6 +347,13 @@ def test_layer_norm(gpu, rows, cols):
     close_enough(P.layer_norm(x), gpu.layer_norm(x), 1e-4, 1e-4)
 
 
+@pytest.mark.parametrize("name", ["ln_readme_16x1024", "ln_readme_5x333"])
+def test_layer_norm_readme_golden(gpu, name):
+    """lcLayerNorm against the reference's own numpy helper (README.md:2267-2270) output."""
+    g = golden(name)
+    close_enough(g["out"], gpu.layer_norm(g["x"]), 1e-4, 1e-4)
+
+
 # ---------------------------------------------------------------- runtime on the device
 def test_device_runtime(gpu):
     L = gpu.lib

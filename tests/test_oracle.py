@@ -90,6 +90,14 @@ def test_layer_norm_formula(P):
     close_enough(ref, P.layer_norm(x), 1e-5, 1e-5)
 
 
+@pytest.mark.parametrize("name", ["ln_readme_16x1024", "ln_readme_5x333"])
+def test_layer_norm_readme_golden(P, name):
+    # Fixtures from the reference's own `_layer_norm_np` (README.md:2267-2270), run by
+    # tests/golden/make_golden.py on np.random.rand-style inputs; numpy reduces in float32.
+    g = golden(name)
+    close_enough(g["out"], P.layer_norm(g["x"]), 2e-5, 2e-5)
+
+
 def test_bf16_round(P):
     x = np.array([1.0, 1.00390625, 1.01171875, -3.14159, 65504.0, 1e-30], np.float32)
     r = P.bf16_round(x)
