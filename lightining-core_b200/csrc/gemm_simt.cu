@@ -4,8 +4,8 @@
 // it) rules out plain TF32 tensor cores, so these kernels accumulate with fp32 FFMA in k order,
 // exactly the reduction order of the reference's i-p-j loop for each output element.
 //
-// Tiling: three CTA tiles (128x128 with 8x8 per thread, 128x64 with 8x8, 64x64 with 4x4), BK = 8,
-// double-buffered shared memory; thread tiles are split into 4-wide strips so every
+// Tiling: three CTA tiles (128x128 with 8x8 per thread, 128x64 with 8x8, both with BK = 8; 64x64
+// with 4x4 and BK = 32), double-buffered shared memory; thread tiles are split into 4-wide strips so every
 // shared-memory read is a conflict-free float4.  The tile comes from the auto-tune cache when it
 // has an entry for the shape, else the largest tile that still gives every SM a CTA.
 // The operands come from loader functors: dense row-major for matmul, an on-the-fly im2col
@@ -20,7 +20,6 @@
 namespace lcb {
 namespace {
 
-constexpr int BK = 8;
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v) { return static_cast<float>(v); }
@@ -95,7 +94,12 @@ struct NchwEpi {
 
 // Tile BM x BN per CTA, thread tile TM x TN (multiples of 4, split into 4-wide strips spaced
 // BM/(TM/4) rows and BN/(TN/4) columns so every shared-memory read is a conflict-free float4).
-template <int BM, int BN, int TM, int TN, class LA, class LB, class Epi>
+// BK: k depth of a shared-memory stage.  The 64x64 tile is the one small problems get (few CTAs,
+// bound by the latency of each stage's loads), so it takes 32-deep stages: a quarter of the
+// load round trips per k; the larger tiles keep 8 (32-deep stages would not fit the 48 KB of
+// static shared memory).
+// The multiply-adds of every output still run in k order, so the results do not depend on BK.
+template <int BM, int BN, int TM, int TN, int BK, class LA, class LB, class Epi>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
     simt_gemm_kernel(LA la, LB lb, Epi epi, int M, int N, int K) {
   constexpr int TX = BN / TN, TY = BM / TM, NT = TX * TY;
@@ -171,11 +175,11 @@ __global__ void __launch_bounds__((BM / TM) * (BN / TN))
   }
 }
 
-template <int BM, int BN, int TM, int TN, class LA, class LB, class Epi>
+template <int BM, int BN, int TM, int TN, int BK, class LA, class LB, class Epi>
 cudaError_t run_tile(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s) {
   dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
   if (grid.y > 65535u) return cudaErrorInvalidConfiguration;
-  simt_gemm_kernel<BM, BN, TM, TN><<<grid, (BM / TM) * (BN / TN), 0, s>>>(la, lb, epi, M, N, K);
+  simt_gemm_kernel<BM, BN, TM, TN, BK><<<grid, (BM / TM) * (BN / TN), 0, s>>>(la, lb, epi, M, N, K);
   return cudaGetLastError();
 }
 
@@ -203,9 +207,9 @@ template <class LA, class LB, class Epi>
 cudaError_t run(LA la, LB lb, Epi epi, int M, int N, int K, cudaStream_t s, int tile = -1) {
   if (tile < 0) tile = default_simt_tile(M, N);
   switch (tile) {
-    case kSimt128x64: return run_tile<128, 64, 8, 8>(la, lb, epi, M, N, K, s);
-    case kSimt64x64: return run_tile<64, 64, 4, 4>(la, lb, epi, M, N, K, s);
-    default: return run_tile<128, 128, 8, 8>(la, lb, epi, M, N, K, s);
+    case kSimt128x64: return run_tile<128, 64, 8, 8, 8>(la, lb, epi, M, N, K, s);
+    case kSimt64x64: return run_tile<64, 64, 4, 4, 32>(la, lb, epi, M, N, K, s);
+    default: return run_tile<128, 128, 8, 8, 8>(la, lb, epi, M, N, K, s);
   }
 }
 
