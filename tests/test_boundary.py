@@ -187,6 +187,26 @@ def test_reference_c_example_links_against_this_library():
     assert "liblc_b200.so" in out and "not found" not in out, out
 
 
+def test_reference_kcuda_route_fails_loudly_without_a_gpu(lc):
+    """The reference's C++ ops called with Device::kCUDA through the integration hooks
+    (tests/native/reference_ops_on_cuda.cpp): on a machine without a visible GPU every kCUDA call
+    comes back as an error (kNotInitialized = 1) instead of kNotSupported, which would send the
+    reference's dispatcher into its silent CPU fallback; the driver exits non-zero."""
+    import subprocess
+
+    exe = os.path.join(ROOT, "oracle", "_ref", "reference_ops_on_cuda")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref/reference_ops_on_cuda not built (needs the reference sources)")
+    if lc.cuda_available():
+        pytest.skip("a GPU is visible: the GPU test runs this driver for real")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode != 0
+    lines = [ln for ln in r.stdout.splitlines() if "cpu=" in ln]
+    assert len(lines) == 5, r.stdout
+    assert all("cpu=0 cuda=1 " in ln for ln in lines), r.stdout
+    assert "served by liblc_b200.so 0" in r.stdout
+
+
 def test_conv_sizes_beyond_int_rejected_before_gpu(lc):
     """The conv launchers work in int: a reduction length in_channels*kh*kw, a padded extent or any
     size argument beyond INT_MAX is LC_NOT_SUPPORTED before anything touches the GPU, in every conv
