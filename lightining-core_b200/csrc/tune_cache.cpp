@@ -58,11 +58,17 @@ const char* columns(int kind) {
                                      : "#columns,channels,spatial,geometry,dtype,config";
 }
 
+// Comma-separated fields with surrounding blanks removed, so files saved with CRLF line ends or
+// padded by hand load the same rows.
 std::vector<std::string> split(const std::string& line) {
   std::vector<std::string> out;
   std::stringstream ss(line);
   std::string f;
-  while (std::getline(ss, f, ',')) out.push_back(f);
+  while (std::getline(ss, f, ',')) {
+    const size_t b = f.find_first_not_of(" \t\r\n");
+    const size_t e = f.find_last_not_of(" \t\r\n");
+    out.push_back(b == std::string::npos ? std::string() : f.substr(b, e - b + 1));
+  }
   return out;
 }
 
@@ -78,8 +84,8 @@ bool load_file(int kind, const std::string& path, std::map<Key, std::string>& in
   if (version != 1 && version != 2) return false;  // unknown format: drop every row
   std::map<Key, std::string> rows;
   while (std::getline(in, line)) {
-    if (line.empty() || line[0] == '#') continue;
     const auto f = split(line);
+    if (f.empty() || f[0].empty() || f[0][0] == '#') continue;
     // v2: d0,d1,d2,dtype,config ; v1 (no dtype column): d0,d1,d2,config with dtype f32.
     if (version == 2 && f.size() == 5) {
       rows[Key{std::strtoull(f[0].c_str(), nullptr, 10), std::strtoull(f[1].c_str(), nullptr, 10),

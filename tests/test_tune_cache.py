@@ -43,6 +43,16 @@ def test_v1_rows_load_as_f32(lc, tmp_path):
     assert lc.tune_cache_get(lc.TUNE_MATMUL, 256, 256, 256) == "simt128x64"
 
 
+def test_crlf_and_padded_rows_load(lc, tmp_path):
+    f = tmp_path / "crlf.csv"
+    f.write_bytes(b"#lc_tune_cache,matmul,2\r\n#columns,m,k,n,dtype,config\r\n"
+                  b"512,512,512,f32,simt64x64\r\n 64 , 32 , 16 , bf16 , tcgen05_128x256 \r\n\r\n")
+    assert lc.lib.lcTuneCacheLoad(lc.TUNE_MATMUL, str(f).encode()) == 0
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 512, 512, 512) == "simt64x64"
+    assert lc.tune_cache_get(lc.TUNE_MATMUL, 64, 32, 16, lc.BF16) == "tcgen05_128x256"
+    assert lc.lib.lcTuneCacheSize(lc.TUNE_MATMUL) == 2
+
+
 @pytest.mark.parametrize("header", ["#lc_tune_cache,matmul,9", "#lc_tune_cache,attention,2", "m,k,n", ""])
 def test_unknown_header_rejected(lc, tmp_path, header):
     lc.tune_cache_set(lc.TUNE_MATMUL, 1, 2, 3, "simt64x64")
