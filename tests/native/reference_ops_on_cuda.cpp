@@ -31,7 +31,8 @@ double excess(const std::vector<float>& want, const std::vector<float>& got, dou
   double worst = -1e300;
   for (std::size_t i = 0; i < want.size(); ++i) {
     const double e = std::fabs(double(got[i]) - double(want[i])) - (atol + rtol * std::fabs(double(want[i])));
-    if (!(e <= worst)) worst = e;  // NaN counts as worst
+    if (std::isnan(e)) return INFINITY;  // a NaN anywhere fails the op
+    if (e > worst) worst = e;
   }
   return worst;
 }
